@@ -1,0 +1,137 @@
+/*
+ * moe_b200.h -- C ABI of the B200 fused-MoE expert engine.
+ *
+ * Plain pointers and sizes only: device pointers are CUDA device addresses,
+ * `stream` is a cudaStream_t passed as void*.  Every entry point returns
+ * MOE_OK (0) or a negative status; moe_last_error() gives the message of the
+ * last failure on the calling thread.  Nothing throws across this boundary.
+ *
+ * Each declaration names the reference interface it replaces
+ * (Qeeweew/MoE-Ascend-Opt, paths relative to that project).
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_OK 0
+#define MOE_ERR_INVALID (-1)   /* bad argument: shape, dtype, pointer, size */
+#define MOE_ERR_CUDA (-2)      /* a CUDA runtime call failed */
+#define MOE_ERR_STATE (-3)     /* call not valid in the engine's state (e.g. no weights) */
+#define MOE_ERR_DEVICE (-4)    /* a kernel reported an error (bounded wait expired) */
+
+/* quant formats: Int8-gemm/quant_traits.h:7-10 (Q8_0 = 0, Q4_0 = 1); AWQ W4A16 is new. */
+#define MOE_Q8_0 0
+#define MOE_Q4_0 1
+#define MOE_AWQ 2
+
+/* element types of activations, scales and weight inputs */
+#define MOE_F16 0
+#define MOE_BF16 1
+#define MOE_F32 2
+
+typedef struct moe_engine moe_engine;
+
+typedef struct moe_config {
+    int64_t num_experts;       /* experts held by this engine (E, or E/ep_size under EP) */
+    int64_t hidden_size;       /* H, multiple of 32 (of the AWQ group for AWQ) */
+    int64_t intermediate_size; /* I, multiple of 32 (of the AWQ group for AWQ) */
+    int32_t quant_type;        /* MOE_Q8_0 / MOE_Q4_0 / MOE_AWQ */
+    int32_t group_size;        /* AWQ group along K (128); ignored otherwise */
+    int32_t device;            /* CUDA device ordinal */
+    int32_t expert_offset;     /* global id of this engine's first expert (EP); 0 otherwise */
+} moe_config;
+
+/* Replaces MoEInfer::MoEInfer (Int8-gemm/moe_infer.cpp:18-75) and the
+ * MoEInfer torch class constructor (Int8-gemm/nanovllm_ops.cpp:23-31).
+ * Checks H % 32 == 0 and I % 32 == 0 as the reference does (moe_infer.cpp:27-31). */
+int moe_engine_create(const moe_config* cfg, moe_engine** out);
+/* Replaces MoEInfer::~MoEInfer (Int8-gemm/moe_infer.cpp:77-84). */
+int moe_engine_destroy(moe_engine* eng);
+
+/* Replaces MoEInfer::store_quantized_weights_repack (Int8-gemm/moe_infer.cpp:96-282).
+ * Row-major input contract (host or device memory, src_on_device says which):
+ *   Q8_0: gate_up_qs int8 [E,2I,H], down_qs int8 [E,H,I]
+ *   Q4_0: gate_up_qs uint32 [E,2I,H/8], down_qs uint32 [E,H,I/8], element k of a row
+ *         at word k/8, bits 4*(k%8), value nibble-8
+ *   scales gate_up_d [E,2I,H/32], down_d [E,H,I/32], both MOE_F16 or both MOE_BF16.
+ * Rows [0,I) of gate_up are gate_proj, rows [I,2I) up_proj. */
+int moe_engine_load_quantized(moe_engine* eng, const void* gate_up_qs, const void* gate_up_d,
+                              const void* down_qs, const void* down_d, int32_t scale_dtype,
+                              int32_t src_on_device, void* stream);
+
+/* Replaces MoEInfer::quantize_and_store_expert (Int8-gemm/moe_infer.cpp:284-360) with
+ * quantize_weight_only (Int8-gemm/q8_gemm.cpp:219-260): Q8_0 only, fp16 scales.
+ * proj: 0 = gate_proj [I,H], 1 = up_proj [I,H], 2 = down_proj [H,I];
+ * w_dtype MOE_F32 / MOE_F16 / MOE_BF16. */
+int moe_engine_quantize_store_expert(moe_engine* eng, int64_t expert, int32_t proj, const void* w,
+                                     int32_t w_dtype, int32_t src_on_device, void* stream);
+
+/* AWQ W4A16 weights (no reference counterpart in this checkout: the Ascend
+ * grouped_gemv kernel of sgl-kernel-npu is absent).  AutoAWQ GEMM packing:
+ *   w13_qweight int32 [E, H, 2I/8], w13_scales bf16 [E, H/G, 2I], w13_qzeros int32 [E, H/G, 2I/8]
+ *   w2_qweight  int32 [E, I, H/8],  w2_scales  bf16 [E, I/G, H],  w2_qzeros  int32 [E, I/G, H/8]
+ * 8 values per int32 in the AWQ order {0,2,4,6,1,3,5,7}; W = (q - z) * s. */
+int moe_engine_load_awq(moe_engine* eng, const void* w13_qweight, const void* w13_scales,
+                        const void* w13_qzeros, const void* w2_qweight, const void* w2_scales,
+                        const void* w2_qzeros, int32_t src_on_device, void* stream);
+
+/* Replaces MoEInfer::execute_on_cpu_routed_from_pointers (Int8-gemm/moe_infer.cpp:430-456)
+ * -> moe_forward_ptr_impl (Int8-gemm/q8_gemm.cpp:276-646).  All pointers on the engine's
+ * device: x [T,H] (act_dtype), y [T,H] (out_dtype: act_dtype, or MOE_F32 for a partial
+ * sum under expert parallelism), topk_ids int32 [T,K], topk_w fp32 [T,K].  Ids outside
+ * this engine's experts are skipped (moe_common.cpp:158,175-181).  Stream ordered. */
+int moe_engine_forward(moe_engine* eng, const void* x, void* y, const int32_t* topk_ids,
+                       const float* topk_w, int64_t num_tokens, int64_t top_k, int32_t act_dtype,
+                       int32_t out_dtype, void* stream);
+
+/* Reserve the forward's device workspace for up to max_tokens x top_k so that
+ * later forwards allocate nothing (needed before CUDA graph capture).
+ * Replaces the role of NumaBufferPool::ensure_capacity (Int8-gemm/moe_common.cpp:57-111). */
+int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t top_k);
+
+/* Device time of the last forward in ms (CUDA events on the forward's stream; waits for
+ * it).  Replaces MoEInfer::get_last_run_time_ms (Int8-gemm/moe_infer.h:24). */
+int moe_engine_last_time_ms(moe_engine* eng, double* ms);
+
+/* Reads and clears the device error word of the engine's workspace (waits for the device).
+ * *code = 0 when every kernel completed; non-zero when a bounded wait expired. */
+int moe_engine_device_error(moe_engine* eng, int32_t* code);
+
+/* Decode the engine's device-resident weights of one expert back into the row-major
+ * input contract (bit-exact check of the load-time packing).  which: 0 gate_up, 1 down.
+ * qs_out / d_out are host buffers of the input-contract sizes. */
+int moe_engine_export_expert(moe_engine* eng, int64_t expert, int32_t which, void* qs_out,
+                             void* d_out);
+
+/* Router (Int8-gemm/test/fused_moe_cpu.py:20-37): top-K of fp32 logits [T,E] in
+ * descending order (ties: lower expert id first), weights = softmax over the K selected
+ * logits (renormalize != 0) or softmax over all E gathered at the selection. */
+int moe_route_topk(const float* logits, int64_t num_tokens, int64_t num_experts, int64_t top_k,
+                   int32_t renormalize, int32_t* topk_ids, float* topk_w, void* stream);
+
+/* Stable counting sort of routed pairs by expert (Int8-gemm/moe_common.cpp:146-216):
+ * counts [E], starts [E+1], token_map [T*K][2] = (t,k) per position, scatter_map [T*K]
+ * (-1 for ids outside [0,E)).  Device pointers. */
+int moe_route_permute(const int32_t* topk_ids, int64_t num_tokens, int64_t top_k,
+                      int64_t num_experts, int32_t* counts, int32_t* starts, int32_t* token_map,
+                      int32_t* scatter_map, void* stream);
+
+/* Q8_0 activation quantisation of rows (Int8-gemm/gemm_kernels.cpp:25-58, stage A of
+ * Int8-gemm/q8_gemm.cpp:360-377): x [rows, cols] (dtype) -> qs int8 [rows, cols],
+ * d fp32 [rows, cols/32].  Device pointers. */
+int moe_quantize_rows_q8_0(const void* x, int32_t dtype, int64_t rows, int64_t cols, int8_t* qs,
+                           float* d, void* stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* moe_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

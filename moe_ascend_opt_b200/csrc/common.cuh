@@ -1,0 +1,153 @@
+// Shared device helpers: element conversions, the SiLU of the reference,
+// mbarrier / bulk-copy PTX wrappers and bounded waits.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define MOE_DEV __device__ __forceinline__
+
+namespace moe {
+
+// Iteration budget of every spin-wait (mbarrier, grid barrier).  With the
+// nanosleep back-off this is on the order of a second; an expired wait sets
+// the workspace error word and the kernel leaves without hanging the GPU.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+enum ErrCode : int32_t { kErrNone = 0, kErrGridBarrier = 1, kErrFullWait = 2, kErrEmptyWait = 3 };
+
+MOE_DEV float act_to_f32(const void* p, int64_t i, int is_bf16) {
+    if (is_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+
+MOE_DEV float scale_to_f32(uint16_t bits, int is_bf16) {
+    if (is_bf16) return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+    return __half2float(__ushort_as_half(bits));
+}
+
+// exp(x) as the reference's vectorised SiLU computes it: the range-reduced
+// polynomial of Int8-gemm/vec_simd.h:9-33, per lane with fused multiply-adds,
+// so that the intermediate activations track the reference bit for bit.
+MOE_DEV float ref_expf(float x) {
+    const float r = 0x1.8p23f;
+    const float z = __fmaf_rn(x, 0x1.715476p+0f, r);
+    const float n = z - r;
+    const float b = __fmaf_rn(-n, 0x1.7f7d1cp-20f, __fmaf_rn(-n, 0x1.62e4p-1f, x));
+    const uint32_t e = __float_as_uint(z) << 23;
+    const float k = __uint_as_float(e + 0x3f800000u);
+    const float u = __fmul_rn(b, b);
+    const float j = __fmaf_rn(__fmaf_rn(__fmaf_rn(0x1.0e4020p-7f, b, 0x1.573e2ep-5f), u,
+                                        __fmaf_rn(0x1.555e66p-3f, b, 0x1.fffdb6p-2f)),
+                              u, __fmul_rn(0x1.ffffecp-1f, b));
+    if (!(fabsf(n) > 126.0f)) return __fmaf_rn(k, j, k);
+    const uint32_t d = (n <= 0.0f) ? 0x82000000u : 0u;
+    const float s1 = __uint_as_float(d + 0x7f000000u);
+    const float s2 = __uint_as_float(e - d);
+    if (fabsf(n) > 192.0f) return __fmul_rn(s1, s1);
+    return __fmul_rn(__fmaf_rn(s2, j, s2), s1);
+}
+
+// SiLU(gate) * up with IEEE division, as Int8-gemm/vec_simd.h:36-64.
+MOE_DEV float silu_mul(float g, float up) {
+    const float act = __fdiv_rn(g, __fadd_rn(1.0f, ref_expf(-g)));
+    return __fmul_rn(up, act);
+}
+
+// One Q8_0 block scale as the reference binary computes it: d = amax * (1/127)
+// (Int8-gemm/gemm_kernels.cpp:43 under -ffast-math), id = d ? 1/d : 0.
+MOE_DEV float q8_scale(float amax) { return __fmul_rn(amax, 1.0f / 127.0f); }
+MOE_DEV float q8_inv(float d) { return d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f; }
+MOE_DEV int q8_quant(float v, float id) {
+    int q = __float2int_rn(__fmul_rn(v, id));  // round to nearest even
+    return q > 127 ? 127 : (q < -128 ? -128 : q);
+}
+
+// ------------------------------------------------------------------ PTX
+MOE_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+MOE_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+MOE_DEV void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+MOE_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+MOE_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+MOE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on a phase of an mbarrier; false when the budget ran out.
+MOE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (it > 64) __nanosleep(64);
+    }
+    return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
+// dst, src and bytes must be multiples of 16.
+MOE_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+MOE_DEV void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+MOE_DEV uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Sense-reversing grid barrier over `nblocks` co-resident CTAs (cooperative launch).
+// bar[0] = arrival count, bar[1] = generation.  Called by one thread per CTA.
+// Returns false (and sets *err) when the wait budget ran out.
+MOE_DEV bool grid_barrier(uint32_t* bar, uint32_t nblocks, int32_t* err) {
+    const uint32_t gen = ld_acquire_gpu(bar + 1);
+    __threadfence();
+    const uint32_t old = atomicAdd(bar, 1u);
+    if (old == nblocks - 1) {
+        atomicExch(bar, 0u);
+        __threadfence();
+        atomicAdd(bar + 1, 1u);
+        return true;
+    }
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        if (ld_acquire_gpu(bar + 1) != gen) return true;
+        __nanosleep(it < 256 ? 20 : 256);
+    }
+    atomicExch(reinterpret_cast<int*>(err), kErrGridBarrier);
+    return false;
+}
+
+}  // namespace moe

@@ -1,0 +1,717 @@
+// C ABI of the fused-MoE expert engine (include/moe_b200.h): engine object,
+// load-time packing of weights into the device layout, workspace, forward
+// dispatch, routing and quantisation entry points.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "awq.cuh"
+#include "common.cuh"
+#include "moe_decode.cuh"
+
+using namespace moe;
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_last_error;
+
+static int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                       \
+    do {                                                                                     \
+        cudaError_t _e = (expr);                                                             \
+        if (_e != cudaSuccess)                                                               \
+            return fail(MOE_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+    } while (0)
+
+extern "C" const char* moe_last_error(void) { return g_last_error.c_str(); }
+
+static inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// ------------------------------------------------------------------ engine
+struct moe_engine {
+    moe_config cfg{};
+    int num_sms = 0;
+    int max_smem = 0;
+    bool loaded = false;
+    int scale_bf16 = 0;
+    // Q8_0 / Q4_0 device layout
+    uint8_t* gu_qs = nullptr;  // [E][I][2][rs1]
+    uint8_t* gu_sc = nullptr;  // [E][I][2][ss1]
+    uint8_t* dn_qs = nullptr;  // [E][H][rs2]
+    uint8_t* dn_sc = nullptr;  // [E][H][ss2]
+    int rs1 = 0, ss1 = 0, rs2 = 0, ss2 = 0;
+    // AWQ device layout
+    AwqWeights awq{};
+    // workspace
+    float* h_ws = nullptr;
+    int64_t h_cap = 0;  // positions
+    uint32_t* bar = nullptr;
+    int32_t* err = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    bool timed = false;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// Copy rows with a row map: dst row d <- src row map(d), `bytes` per row,
+// destination rows padded with zeros to `dstride`.
+enum RowMap { kIdentity = 0, kGateUpInterleave = 1 };
+
+__global__ void pack_rows_kernel(uint8_t* dst, const uint8_t* src, int64_t nrows, int64_t bytes,
+                                 int64_t dstride, int64_t sstride, int map, int64_t I) {
+    const int64_t row = blockIdx.x;
+    if (row >= nrows) return;
+    int64_t srow = row;
+    if (map == kGateUpInterleave) {  // dst row = (e*I + j)*2 + r ; src row = e*2I + r*I + j
+        const int64_t r = row & 1, ej = row >> 1, e = ej / I, j = ej % I;
+        srow = e * 2 * I + r * I + j;
+    }
+    const uint8_t* s = src + srow * sstride;
+    uint8_t* d = dst + row * dstride;
+    for (int64_t c = threadIdx.x; c < dstride; c += blockDim.x) d[c] = c < bytes ? s[c] : 0;
+}
+
+// Inverse of pack_rows_kernel for one expert (export / bit-exact decode check).
+__global__ void unpack_rows_kernel(uint8_t* dst, const uint8_t* src, int64_t nrows, int64_t bytes,
+                                   int64_t sstride, int map, int64_t I) {
+    const int64_t srow = blockIdx.x;  // row in the packed (destination-layout) buffer
+    if (srow >= nrows) return;
+    int64_t drow = srow;
+    if (map == kGateUpInterleave) {
+        const int64_t r = srow & 1, j = srow >> 1;
+        drow = r * I + j;
+    }
+    for (int64_t c = threadIdx.x; c < bytes; c += blockDim.x) dst[drow * bytes + c] = src[srow * sstride + c];
+}
+
+// Online Q8_0 quantisation of one weight matrix [rows, cols] straight into the
+// device layout (quantize_weight_only, Int8-gemm/q8_gemm.cpp:197-260: fp16 scale).
+__global__ void quantize_weight_rows_kernel(const void* w, int w_dtype, int64_t rows, int64_t cols,
+                                            uint8_t* qs_base, int64_t qs_row_stride, int64_t qs_row_step,
+                                            uint8_t* sc_base, int64_t sc_row_stride, int64_t sc_row_step) {
+    // one warp per 32-block; lane = element
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = cols / 32;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= rows * nb) return;
+    const int64_t r = gw / nb, b = gw % nb;
+    const int64_t i = r * cols + b * 32 + lane;
+    float v;
+    if (w_dtype == MOE_F32) v = reinterpret_cast<const float*>(w)[i];
+    else if (w_dtype == MOE_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(w)[i]);
+    else v = __half2float(reinterpret_cast<const __half*>(w)[i]);
+    float amax = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = q8_scale(amax);
+    const float id = q8_inv(d);
+    uint8_t* qrow = qs_base + r * qs_row_step * qs_row_stride;
+    qrow[b * 32 + lane] = (uint8_t)(int8_t)q8_quant(v, id);
+    if (lane == 0) {
+        uint16_t* srow = reinterpret_cast<uint16_t*>(sc_base + r * sc_row_step * sc_row_stride);
+        srow[b] = __half_as_ushort(__float2half_rn(d));
+    }
+}
+
+__global__ void quantize_rows_kernel(const void* x, int dtype, int64_t rows, int64_t cols, int8_t* qs, float* d) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = cols / 32;
+    const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= rows * nb) return;
+    const int64_t i = gw * 32 + lane;  // rows are contiguous: block gw covers [gw*32, gw*32+32)
+    float v;
+    if (dtype == MOE_F32) v = reinterpret_cast<const float*>(x)[i];
+    else v = act_to_f32(x, i, dtype == MOE_BF16);
+    float amax = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float dd = q8_scale(amax);
+    qs[i] = (int8_t)q8_quant(v, q8_inv(dd));
+    if (lane == 0) d[gw] = dd;
+}
+
+// Standalone stable permutation (one warp, global memory), moe_route_permute.
+__global__ void route_permute_kernel(const int32_t* ids, int TK, int E, int32_t* counts, int32_t* starts,
+                                     int32_t* token_map, int32_t* scatter_map, int32_t* tmp_ids) {
+    const int lane = threadIdx.x;
+    RouteSmem r;
+    r.ids = tmp_ids;
+    r.smap = scatter_map;
+    r.tok = token_map + TK;  // second half as pair-index scratch; rewritten below
+    r.cnt = counts;
+    r.start = starts;
+    r.ue = r.ups = r.ucnt = nullptr;
+    r.nuniq = nullptr;
+    // counts + ranks
+    for (int e = lane; e < E; e += 32) r.cnt[e] = 0;
+    __syncwarp();
+    for (int i0 = 0; i0 < TK; i0 += 32) {
+        const int i = i0 + lane;
+        int e = -1;
+        if (i < TK) {
+            const int g = ids[i];
+            e = (g >= 0 && g < E) ? g : -1;
+            r.ids[i] = e;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        int base = 0;
+        if (e >= 0) base = r.cnt[e];
+        __syncwarp();
+        if (i < TK) r.smap[i] = (e >= 0) ? base + rank : -1;
+        if (e >= 0 && rank == 0) r.cnt[e] = base + __popc(peers);
+        __syncwarp();
+        __threadfence_block();
+    }
+    int carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+        const int e = e0 + lane;
+        const int c = (e < E) ? r.cnt[e] : 0;
+        int incl = c;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (e < E) r.start[e] = carry + incl - c;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) r.start[E] = carry;
+    __syncwarp();
+    __threadfence_block();
+    for (int i = lane; i < TK; i += 32) {
+        const int e = r.ids[i];
+        if (e >= 0) r.smap[i] = r.start[e] + r.smap[i];
+    }
+    __syncwarp();
+    __threadfence_block();
+}
+
+__global__ void token_map_kernel(const int32_t* scatter_map, int TK, int K, int32_t* token_map) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= TK) return;
+    const int pos = scatter_map[i];
+    if (pos >= 0) {
+        token_map[2 * pos] = i / K;
+        token_map[2 * pos + 1] = i % K;
+    }
+}
+
+// Router: one warp per token; K rounds of warp argmax (ties -> lower id).
+__global__ void route_topk_kernel(const float* logits, int T, int E, int K, int renorm, int32_t* ids,
+                                  float* w) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const float* l = logits + (size_t)warp * E;
+    extern __shared__ uint32_t taken_all[];
+    uint32_t* taken = taken_all + (threadIdx.x >> 5) * ((E + 31) / 32);
+    for (int i = lane; i < (E + 31) / 32; i += 32) taken[i] = 0;
+    __syncwarp();
+    float sel_v[16];
+    int sel_i[16];
+    for (int k = 0; k < K; ++k) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < E; e += 32) {
+            if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
+            const float v = l[e];
+            if (bi == 0x7fffffff || v > bv) { bv = v; bi = e; }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) taken[bi >> 5] |= 1u << (bi & 31);
+        __syncwarp();
+        if (k < 16) { sel_v[k] = bv; sel_i[k] = bi; }
+    }
+    if (lane == 0) {
+        float m, s = 0.f;
+        if (renorm) {
+            m = sel_v[0];
+            for (int k = 0; k < K; ++k) s += expf(sel_v[k] - m);
+            for (int k = 0; k < K; ++k) {
+                ids[(size_t)warp * K + k] = sel_i[k];
+                w[(size_t)warp * K + k] = expf(sel_v[k] - m) / s;
+            }
+        } else {
+            m = sel_v[0];  // the overall maximum
+            for (int e = 0; e < E; ++e) s += expf(l[e] - m);
+            for (int k = 0; k < K; ++k) {
+                ids[(size_t)warp * K + k] = sel_i[k];
+                w[(size_t)warp * K + k] = expf(sel_v[k] - m) / s;
+            }
+        }
+    }
+}
+
+int check_engine(moe_engine* eng) {
+    if (!eng) return fail(MOE_ERR_INVALID, "engine is null");
+    return MOE_OK;
+}
+
+// Copy a host or device source to a fresh device buffer (or alias it).
+int stage_to_device(const void* src, size_t bytes, int on_device, cudaStream_t st, const uint8_t** out,
+                    uint8_t** owned) {
+    *owned = nullptr;
+    if (on_device) {
+        *out = static_cast<const uint8_t*>(src);
+        return MOE_OK;
+    }
+    uint8_t* d = nullptr;
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&d), bytes ? bytes : 16, st));
+    CUDA_TRY(cudaMemcpyAsync(d, src, bytes, cudaMemcpyHostToDevice, st));
+    *owned = d;
+    *out = d;
+    return MOE_OK;
+}
+
+int alloc_q_layout(moe_engine* eng) {
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    const bool q4 = eng->cfg.quant_type == MOE_Q4_0;
+    eng->rs1 = (int)round_up(q4 ? H / 2 : H, 16);
+    eng->ss1 = (int)round_up((H / 32) * 2, 16);
+    eng->rs2 = (int)round_up(q4 ? I / 2 : I, 16);
+    eng->ss2 = (int)round_up((I / 32) * 2, 16);
+    if (!eng->gu_qs) {
+        CUDA_TRY(cudaMalloc(&eng->gu_qs, (size_t)E * I * 2 * eng->rs1));
+        CUDA_TRY(cudaMalloc(&eng->gu_sc, (size_t)E * I * 2 * eng->ss1));
+        CUDA_TRY(cudaMalloc(&eng->dn_qs, (size_t)E * H * eng->rs2));
+        CUDA_TRY(cudaMalloc(&eng->dn_sc, (size_t)E * H * eng->ss2));
+        CUDA_TRY(cudaMemset(eng->gu_qs, 0, (size_t)E * I * 2 * eng->rs1));
+        CUDA_TRY(cudaMemset(eng->gu_sc, 0, (size_t)E * I * 2 * eng->ss1));
+        CUDA_TRY(cudaMemset(eng->dn_qs, 0, (size_t)E * H * eng->rs2));
+        CUDA_TRY(cudaMemset(eng->dn_sc, 0, (size_t)E * H * eng->ss2));
+    }
+    return MOE_OK;
+}
+
+int ensure_workspace(moe_engine* eng, int64_t positions) {
+    if (!eng->bar) {
+        CUDA_TRY(cudaMalloc(&eng->bar, 256));
+        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
+        eng->err = reinterpret_cast<int32_t*>(eng->bar + 16);
+    }
+    if (positions <= eng->h_cap) return MOE_OK;
+    int64_t cap = eng->h_cap ? eng->h_cap : 64;
+    while (cap < positions) cap *= 2;
+    if (eng->h_ws) CUDA_TRY(cudaFree(eng->h_ws));
+    eng->h_ws = nullptr;
+    CUDA_TRY(cudaMalloc(&eng->h_ws, (size_t)cap * eng->cfg.intermediate_size * sizeof(float)));
+    eng->h_cap = cap;
+    return MOE_OK;
+}
+
+// Shared-memory plan of the decode kernel for T tokens; false if it does not fit.
+struct DecodePlan {
+    DecodeParams p;
+    size_t smem;
+    int grid;
+};
+
+bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    const int TK = T * K, nb1 = H / 32, nb2 = I / 32;
+    const int G = eng->num_sms;
+    DecodeParams& p = pl.p;
+    std::memset(&p, 0, sizeof(p));
+    int64_t off = round_up((int64_t)(3 * TK + 5 * E + 4) * 4, 128);
+    p.off_x = (int)off;
+    const int64_t xbytes = round_up((int64_t)T * H, 16) + (int64_t)T * nb1 * 8;
+    const int64_t hbytes = round_up((int64_t)TK * I, 16) + (int64_t)TK * nb2 * 8;
+    off += round_up(std::max(xbytes, hbytes), 128);
+    p.off_out = (int)off;
+    p.rows_max = (H + G - 1) / G;
+    off += round_up((int64_t)TK * p.rows_max * 4, 128);
+    const int64_t unit_bytes = 2 * (int64_t)(eng->rs1 + eng->ss1);
+    const int64_t row2_bytes = (int64_t)p.rows_max * (eng->rs2 + eng->ss2);
+    int64_t stage = std::max<int64_t>(32768, std::max(unit_bytes, row2_bytes));
+    stage = round_up(stage, 128);
+    const int64_t avail = (int64_t)eng->max_smem - off - 128;  // room for mbarriers
+    int ns = (int)std::min<int64_t>(8, avail / (stage + 16));
+    if (ns < 2) return false;
+    p.nstages = ns;
+    p.stage_bytes = (int)stage;
+    off = round_up(off + 16 * ns, 128);
+    p.off_stage = (int)off;
+    // barriers sit in the 16*ns bytes right before off_stage
+    off += (int64_t)ns * stage;
+    if (off > eng->max_smem) return false;
+    p.units_per_chunk = (int)std::max<int64_t>(1, stage / unit_bytes);
+    p.experts_per_chunk = (int)std::max<int64_t>(1, stage / std::max<int64_t>(1, row2_bytes));
+    int lpr = 32;
+    while (lpr > 1 && nb2 % lpr != 0) lpr >>= 1;
+    p.lanes_per_row = lpr;
+    p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
+    p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
+    p.scale_bf16 = eng->scale_bf16;
+    pl.smem = (size_t)off;
+    pl.grid = G;
+    return true;
+}
+
+template <bool Q4>
+int launch_decode(const DecodePlan& pl, cudaStream_t st) {
+    auto kern = moe_decode_kernel<Q4>;
+    static thread_local int smem_set[64] = {};  // per device: largest opt-in already applied
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && smem_set[dev] < (int)pl.smem) {
+        CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+        smem_set[dev] = (int)pl.smem;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, pl.p));
+    return MOE_OK;
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
+    if (!cfg || !out) return fail(MOE_ERR_INVALID, "null argument");
+    *out = nullptr;
+    const int64_t E = cfg->num_experts, H = cfg->hidden_size, I = cfg->intermediate_size;
+    if (E <= 0 || H <= 0 || I <= 0) return fail(MOE_ERR_INVALID, "E, H, I must be positive");
+    if (H % 32 != 0) return fail(MOE_ERR_INVALID, "hidden_size must be multiple of 32");
+    if (I % 32 != 0) return fail(MOE_ERR_INVALID, "intermediate_size must be multiple of 32");
+    if (cfg->quant_type < MOE_Q8_0 || cfg->quant_type > MOE_AWQ)
+        return fail(MOE_ERR_INVALID, "quant_type must be 0 (Q8_0), 1 (Q4_0) or 2 (AWQ)");
+    if (cfg->quant_type == MOE_AWQ) {
+        const int g = cfg->group_size;
+        if (g <= 0 || g % 32 != 0 || H % g != 0 || I % g != 0)
+            return fail(MOE_ERR_INVALID, "AWQ group_size must be a multiple of 32 dividing H and I");
+    }
+    int ndev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&ndev));
+    if (cfg->device < 0 || cfg->device >= ndev) return fail(MOE_ERR_INVALID, "device ordinal out of range");
+    DeviceGuard g(cfg->device);
+    auto* eng = new moe_engine();
+    eng->cfg = *cfg;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, cfg->device) != cudaSuccess) {
+        delete eng;
+        return fail(MOE_ERR_CUDA, "cudaGetDeviceProperties failed");
+    }
+    eng->num_sms = prop.multiProcessorCount;
+    eng->max_smem = (int)prop.sharedMemPerBlockOptin;
+    int rc = MOE_OK;
+    if (cfg->quant_type == MOE_AWQ) rc = awq_alloc(eng->awq, E, H, I, cfg->group_size);
+    else rc = alloc_q_layout(eng);
+    if (rc == MOE_OK) rc = ensure_workspace(eng, 64);
+    if (rc == MOE_OK && (cudaEventCreate(&eng->ev0) != cudaSuccess || cudaEventCreate(&eng->ev1) != cudaSuccess))
+        rc = fail(MOE_ERR_CUDA, "cudaEventCreate failed");
+    if (rc != MOE_OK) {
+        moe_engine_destroy(eng);
+        return rc;
+    }
+    *out = eng;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_destroy(moe_engine* eng) {
+    if (!eng) return MOE_OK;
+    DeviceGuard g(eng->cfg.device);
+    cudaFree(eng->gu_qs);
+    cudaFree(eng->gu_sc);
+    cudaFree(eng->dn_qs);
+    cudaFree(eng->dn_sc);
+    awq_free(eng->awq);
+    cudaFree(eng->h_ws);
+    cudaFree(eng->bar);
+    if (eng->ev0) cudaEventDestroy(eng->ev0);
+    if (eng->ev1) cudaEventDestroy(eng->ev1);
+    delete eng;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_load_quantized(moe_engine* eng, const void* gu_qs, const void* gu_d, const void* dn_qs,
+                                         const void* dn_d, int32_t scale_dtype, int32_t src_on_device,
+                                         void* stream) {
+    if (int rc = check_engine(eng)) return rc;
+    if (eng->cfg.quant_type == MOE_AWQ) return fail(MOE_ERR_STATE, "AWQ engine: use moe_engine_load_awq");
+    if (!gu_qs || !gu_d || !dn_qs || !dn_d) return fail(MOE_ERR_INVALID, "null weight pointer");
+    if (scale_dtype != MOE_F16 && scale_dtype != MOE_BF16)
+        return fail(MOE_ERR_INVALID, "scales must be float16 or bfloat16");
+    DeviceGuard g(eng->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    const bool q4 = eng->cfg.quant_type == MOE_Q4_0;
+    const int64_t gu_row = q4 ? H / 2 : H, dn_row = q4 ? I / 2 : I;
+    struct Piece { const void* src; size_t bytes; int64_t rows, row_bytes, dstride; uint8_t* dst; int map; };
+    Piece pieces[4] = {
+        {gu_qs, (size_t)E * 2 * I * gu_row, E * 2 * I, gu_row, eng->rs1, eng->gu_qs, kGateUpInterleave},
+        {gu_d, (size_t)E * 2 * I * (H / 32) * 2, E * 2 * I, (H / 32) * 2, eng->ss1, eng->gu_sc, kGateUpInterleave},
+        {dn_qs, (size_t)E * H * dn_row, E * H, dn_row, eng->rs2, eng->dn_qs, kIdentity},
+        {dn_d, (size_t)E * H * (I / 32) * 2, E * H, (I / 32) * 2, eng->ss2, eng->dn_sc, kIdentity},
+    };
+    for (auto& pc : pieces) {
+        const uint8_t* src = nullptr;
+        uint8_t* owned = nullptr;
+        if (int rc = stage_to_device(pc.src, pc.bytes, src_on_device, st, &src, &owned)) return rc;
+        pack_rows_kernel<<<(unsigned)pc.rows, 128, 0, st>>>(pc.dst, src, pc.rows, pc.row_bytes, pc.dstride,
+                                                             pc.row_bytes, pc.map, I);
+        CUDA_TRY(cudaGetLastError());
+        if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
+    }
+    CUDA_TRY(cudaStreamSynchronize(st));
+    eng->scale_bf16 = scale_dtype == MOE_BF16;
+    eng->loaded = true;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_quantize_store_expert(moe_engine* eng, int64_t expert, int32_t proj, const void* w,
+                                                int32_t w_dtype, int32_t src_on_device, void* stream) {
+    if (int rc = check_engine(eng)) return rc;
+    if (eng->cfg.quant_type != MOE_Q8_0)
+        return fail(MOE_ERR_STATE, "online quantization is Q8_0 only; use store_quantized_repack()");
+    if (!w) return fail(MOE_ERR_INVALID, "null weight");
+    if (w_dtype != MOE_F32 && w_dtype != MOE_F16 && w_dtype != MOE_BF16)
+        return fail(MOE_ERR_INVALID, "weight must be float32, float16 or bfloat16");
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    if (expert < 0 || expert >= E) return fail(MOE_ERR_INVALID, "expert index out of range");
+    if (proj < 0 || proj > 2) return fail(MOE_ERR_INVALID, "Unknown proj_name");
+    if (eng->loaded && eng->scale_bf16) return fail(MOE_ERR_STATE, "engine holds bfloat16 scales");
+    DeviceGuard g(eng->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t rows = proj == 2 ? H : I, cols = proj == 2 ? I : H;
+    const size_t esz = w_dtype == MOE_F32 ? 4 : 2;
+    const uint8_t* src = nullptr;
+    uint8_t* owned = nullptr;
+    if (int rc = stage_to_device(w, (size_t)rows * cols * esz, src_on_device, st, &src, &owned)) return rc;
+    uint8_t *qb, *sb;
+    int64_t qstride, sstride, step;
+    if (proj == 2) {
+        qb = eng->dn_qs + (size_t)expert * H * eng->rs2;
+        sb = eng->dn_sc + (size_t)expert * H * eng->ss2;
+        qstride = eng->rs2; sstride = eng->ss2; step = 1;
+    } else {
+        qb = eng->gu_qs + ((size_t)expert * I * 2 + proj) * eng->rs1;
+        sb = eng->gu_sc + ((size_t)expert * I * 2 + proj) * eng->ss1;
+        qstride = eng->rs1; sstride = eng->ss1; step = 2;
+    }
+    const int64_t warps = rows * (cols / 32);
+    quantize_weight_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+        src, w_dtype, rows, cols, qb, qstride, step, sb, sstride, step);
+    CUDA_TRY(cudaGetLastError());
+    if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    eng->scale_bf16 = 0;
+    eng->loaded = true;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_load_awq(moe_engine* eng, const void* w13_qw, const void* w13_sc, const void* w13_qz,
+                                   const void* w2_qw, const void* w2_sc, const void* w2_qz, int32_t src_on_device,
+                                   void* stream) {
+    if (int rc = check_engine(eng)) return rc;
+    if (eng->cfg.quant_type != MOE_AWQ) return fail(MOE_ERR_STATE, "not an AWQ engine");
+    if (!w13_qw || !w13_sc || !w13_qz || !w2_qw || !w2_sc || !w2_qz) return fail(MOE_ERR_INVALID, "null weight");
+    DeviceGuard g(eng->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    const int64_t G = eng->cfg.group_size;
+    const void* srcs[6] = {w13_qw, w13_sc, w13_qz, w2_qw, w2_sc, w2_qz};
+    const size_t sizes[6] = {(size_t)E * H * (2 * I / 8) * 4, (size_t)E * (H / G) * 2 * I * 2,
+                             (size_t)E * (H / G) * (2 * I / 8) * 4, (size_t)E * I * (H / 8) * 4,
+                             (size_t)E * (I / G) * H * 2, (size_t)E * (I / G) * (H / 8) * 4};
+    const uint8_t* dev[6];
+    uint8_t* owned[6] = {};
+    for (int i = 0; i < 6; ++i)
+        if (int rc = stage_to_device(srcs[i], sizes[i], src_on_device, st, &dev[i], &owned[i])) return rc;
+    int rc = awq_pack(eng->awq, dev, st);
+    for (int i = 0; i < 6; ++i)
+        if (owned[i]) cudaFreeAsync(owned[i], st);
+    if (rc) return fail(MOE_ERR_CUDA, std::string("AWQ pack: ") + cudaGetErrorString(cudaGetLastError()));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    eng->loaded = true;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t top_k) {
+    if (int rc = check_engine(eng)) return rc;
+    if (max_tokens < 0 || top_k <= 0) return fail(MOE_ERR_INVALID, "bad reserve size");
+    DeviceGuard g(eng->cfg.device);
+    return ensure_workspace(eng, max_tokens * top_k);
+}
+
+extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const int32_t* topk_ids,
+                                  const float* topk_w, int64_t T, int64_t K, int32_t act_dtype, int32_t out_dtype,
+                                  void* stream) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!eng->loaded) return fail(MOE_ERR_STATE, "no weights loaded");
+    if (T < 0 || K <= 0 || K > 64) return fail(MOE_ERR_INVALID, "num_tokens must be >= 0 and 1 <= top_k <= 64");
+    if (act_dtype != MOE_F16 && act_dtype != MOE_BF16) return fail(MOE_ERR_INVALID, "hidden must be f16 or bf16");
+    if (out_dtype != MOE_F16 && out_dtype != MOE_BF16 && out_dtype != MOE_F32)
+        return fail(MOE_ERR_INVALID, "bad output dtype");
+    if (T > 0 && (!x || !y || !topk_ids || !topk_w)) return fail(MOE_ERR_INVALID, "null tensor pointer");
+    DeviceGuard g(eng->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (T == 0) return MOE_OK;
+    const int64_t H = eng->cfg.hidden_size;
+    const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
+    if (eng->cfg.quant_type == MOE_AWQ) {
+        if (int rc = ensure_workspace(eng, T * K)) return rc;
+        CUDA_TRY(cudaEventRecord(eng->ev0, st));
+        int rc = awq_forward(eng->awq, eng->num_sms, eng->max_smem, (int)eng->cfg.expert_offset, x, y, topk_ids,
+                             topk_w, (int)T, (int)K, act_dtype == MOE_BF16, out_dtype, eng->h_ws, eng->bar, eng->err,
+                             st);
+        if (rc) return fail(MOE_ERR_CUDA, std::string("AWQ forward: ") + cudaGetErrorString(cudaGetLastError()));
+        CUDA_TRY(cudaEventRecord(eng->ev1, st));
+        eng->timed = true;
+        return MOE_OK;
+    }
+    // token slice that fits the decode kernel's shared-memory plan
+    int64_t slice = T;
+    DecodePlan pl;
+    while (slice > 0 && !plan_decode(eng, (int)slice, (int)K, pl)) slice = slice > 8 ? slice / 2 : slice - 1;
+    if (slice == 0) return fail(MOE_ERR_INVALID, "shapes exceed the decode kernel's shared memory");
+    if (int rc = ensure_workspace(eng, slice * K)) return rc;
+    CUDA_TRY(cudaEventRecord(eng->ev0, st));
+    for (int64_t t0 = 0; t0 < T; t0 += slice) {
+        const int64_t n = std::min(slice, T - t0);
+        if (n != slice && !plan_decode(eng, (int)n, (int)K, pl)) return fail(MOE_ERR_INVALID, "plan failed");
+        DecodeParams& p = pl.p;
+        p.T = (int)n;
+        p.act_bf16 = act_dtype == MOE_BF16;
+        p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+        p.x = static_cast<const uint8_t*>(x) + (size_t)t0 * H * xe;
+        p.y = static_cast<uint8_t*>(y) + (size_t)t0 * H * ye;
+        p.ids = topk_ids + t0 * K;
+        p.tw = topk_w + t0 * K;
+        p.gu_qs = eng->gu_qs; p.gu_sc = eng->gu_sc; p.dn_qs = eng->dn_qs; p.dn_sc = eng->dn_sc;
+        p.h_ws = eng->h_ws; p.bar = eng->bar; p.err = eng->err;
+        const int rc = eng->cfg.quant_type == MOE_Q4_0 ? launch_decode<true>(pl, st) : launch_decode<false>(pl, st);
+        if (rc) return rc;
+    }
+    CUDA_TRY(cudaEventRecord(eng->ev1, st));
+    eng->timed = true;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_last_time_ms(moe_engine* eng, double* ms) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!ms) return fail(MOE_ERR_INVALID, "null output");
+    *ms = 0.0;
+    if (!eng->timed) return MOE_OK;
+    DeviceGuard g(eng->cfg.device);
+    CUDA_TRY(cudaEventSynchronize(eng->ev1));
+    float f = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&f, eng->ev0, eng->ev1));
+    *ms = f;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_device_error(moe_engine* eng, int32_t* code) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!code) return fail(MOE_ERR_INVALID, "null output");
+    DeviceGuard g(eng->cfg.device);
+    CUDA_TRY(cudaDeviceSynchronize());
+    int32_t v = 0;
+    CUDA_TRY(cudaMemcpy(&v, eng->err, 4, cudaMemcpyDeviceToHost));
+    *code = v;
+    if (v != 0) CUDA_TRY(cudaMemset(eng->bar, 0, 256));  // clear error word and barrier state
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_export_expert(moe_engine* eng, int64_t expert, int32_t which, void* qs_out,
+                                        void* d_out) {
+    if (int rc = check_engine(eng)) return rc;
+    if (eng->cfg.quant_type == MOE_AWQ) return fail(MOE_ERR_STATE, "export is for Q8_0/Q4_0 engines");
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    if (expert < 0 || expert >= E || (which != 0 && which != 1) || !qs_out || !d_out)
+        return fail(MOE_ERR_INVALID, "bad export argument");
+    DeviceGuard g(eng->cfg.device);
+    const bool q4 = eng->cfg.quant_type == MOE_Q4_0;
+    const int64_t rows = which == 0 ? 2 * I : H;
+    const int64_t qrow = which == 0 ? (q4 ? H / 2 : H) : (q4 ? I / 2 : I);
+    const int64_t srow = which == 0 ? (H / 32) * 2 : (I / 32) * 2;
+    const uint8_t* qsrc = which == 0 ? eng->gu_qs + (size_t)expert * rows * eng->rs1 : eng->dn_qs + (size_t)expert * rows * eng->rs2;
+    const uint8_t* ssrc = which == 0 ? eng->gu_sc + (size_t)expert * rows * eng->ss1 : eng->dn_sc + (size_t)expert * rows * eng->ss2;
+    uint8_t *dq = nullptr, *ds = nullptr;
+    CUDA_TRY(cudaMalloc(&dq, rows * qrow));
+    CUDA_TRY(cudaMalloc(&ds, rows * srow));
+    const int map = which == 0 ? kGateUpInterleave : kIdentity;
+    unpack_rows_kernel<<<(unsigned)rows, 128>>>(dq, qsrc, rows, qrow, which == 0 ? eng->rs1 : eng->rs2, map, I);
+    unpack_rows_kernel<<<(unsigned)rows, 128>>>(ds, ssrc, rows, srow, which == 0 ? eng->ss1 : eng->ss2, map, I);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaMemcpy(qs_out, dq, rows * qrow, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(d_out, ds, rows * srow, cudaMemcpyDeviceToHost));
+    cudaFree(dq);
+    cudaFree(ds);
+    return MOE_OK;
+}
+
+extern "C" int moe_route_topk(const float* logits, int64_t T, int64_t E, int64_t K, int32_t renorm, int32_t* ids,
+                              float* w, void* stream) {
+    if (T < 0 || E <= 0 || K <= 0 || K > 16 || K > E) return fail(MOE_ERR_INVALID, "need 1 <= top_k <= min(16, E)");
+    if (E > 4096) return fail(MOE_ERR_INVALID, "num_experts > 4096");
+    if (T == 0) return MOE_OK;
+    if (!logits || !ids || !w) return fail(MOE_ERR_INVALID, "null pointer");
+    const int wpb = 4;
+    const size_t smem = (size_t)wpb * ((E + 31) / 32) * 4;
+    route_topk_kernel<<<(unsigned)((T + wpb - 1) / wpb), wpb * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+        logits, (int)T, (int)E, (int)K, renorm, ids, w);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+extern "C" int moe_route_permute(const int32_t* ids, int64_t T, int64_t K, int64_t E, int32_t* counts, int32_t* starts,
+                                 int32_t* token_map, int32_t* scatter_map, void* stream) {
+    if (T < 0 || K <= 0 || E <= 0) return fail(MOE_ERR_INVALID, "bad sizes");
+    if (!counts || !starts || (T > 0 && (!ids || !token_map || !scatter_map)))
+        return fail(MOE_ERR_INVALID, "null pointer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int TK = (int)(T * K);
+    int32_t* tmp = nullptr;
+    CUDA_TRY(cudaMallocAsync(&tmp, (size_t)std::max(TK, 1) * 4, st));
+    route_permute_kernel<<<1, 32, 0, st>>>(ids, TK, (int)E, counts, starts, token_map, scatter_map, tmp);
+    CUDA_TRY(cudaGetLastError());
+    if (TK > 0) {
+        token_map_kernel<<<(TK + 255) / 256, 256, 0, st>>>(scatter_map, TK, (int)K, token_map);
+        CUDA_TRY(cudaGetLastError());
+    }
+    CUDA_TRY(cudaFreeAsync(tmp, st));
+    return MOE_OK;
+}
+
+extern "C" int moe_quantize_rows_q8_0(const void* x, int32_t dtype, int64_t rows, int64_t cols, int8_t* qs, float* d,
+                                      void* stream) {
+    if (rows < 0 || cols <= 0 || cols % 32 != 0) return fail(MOE_ERR_INVALID, "cols must be a positive multiple of 32");
+    if (dtype != MOE_F16 && dtype != MOE_BF16 && dtype != MOE_F32) return fail(MOE_ERR_INVALID, "bad dtype");
+    if (rows == 0) return MOE_OK;
+    if (!x || !qs || !d) return fail(MOE_ERR_INVALID, "null pointer");
+    const int64_t warps = rows * (cols / 32);
+    quantize_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, dtype, rows, cols, qs, d);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}

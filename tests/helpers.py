@@ -1,0 +1,49 @@
+"""Seeded synthetic inputs and parity metrics shared by the tests."""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import oracle as O
+
+# North-star tolerance for the FFN output (bf16 in / fp32 accumulate).
+MAX_REL = 1e-2
+MIN_COS = 0.9999
+
+
+def parity(y: np.ndarray, y_ref: np.ndarray):
+    """(normwise max rel err, cosine) of y against y_ref."""
+    y = np.asarray(y, np.float64).ravel()
+    r = np.asarray(y_ref, np.float64).ravel()
+    den = np.abs(r).max()
+    rel = float(np.abs(y - r).max() / den) if den > 0 else float(np.abs(y).max())
+    nr, ny = np.linalg.norm(r), np.linalg.norm(y)
+    cos = float(np.dot(y, r) / (nr * ny)) if nr > 0 and ny > 0 else (1.0 if nr == ny else 0.0)
+    return rel, cos
+
+
+def q_weights(qt: int, E: int, H: int, I: int, seed: int, scale_bf16: bool = False, std: float = 0.02):
+    """Row-major quantised weights: fp32 N(0, std^2) -> Q8_0 (reference rule) or Q4_0 (harness rule)."""
+    rng = np.random.default_rng(seed)
+    wg = (rng.standard_normal((E, 2 * I, H), dtype=np.float32) * std).astype(np.float32)
+    wd = (rng.standard_normal((E, H, I), dtype=np.float32) * std).astype(np.float32)
+    if qt == 0:
+        gq, gd = O.quantize_weight_q8_0(wg)
+        dq, dd = O.quantize_weight_q8_0(wd)
+    else:
+        gq, gd = O.quantize_weight_q4_0(wg)
+        dq, dd = O.quantize_weight_q4_0(wd)
+    if scale_bf16:
+        gd = O.f32_to_bf16_bits(O.f16_bits_to_f32(gd))
+        dd = O.f32_to_bf16_bits(O.f16_bits_to_f32(dd))
+    return gq, gd, dq, dd
+
+
+def tokens(T: int, H: int, E: int, K: int, seed: int, bf16: bool = True):
+    """(x bits uint16 [T,H], x as fp32, topk ids [T,K], topk weights [T,K]) with softmax-top-K routing."""
+    rng = np.random.default_rng(seed + 7919)
+    xf = rng.standard_normal((T, H), dtype=np.float32)
+    bits = O.f32_to_bf16_bits(xf) if bf16 else O.f32_to_f16_bits(xf)
+    xf = O.bf16_bits_to_f32(bits) if bf16 else O.f16_bits_to_f32(bits)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    ids, w = O.topk_softmax(logits, K, True)
+    return bits, xf, ids, w
