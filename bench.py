@@ -1,0 +1,499 @@
+"""Benchmark of the fused MoE expert layer (one JSON line on stdout, rank 0).
+
+Workload (N=1): BASELINE configs[1] -- Q4_0 fused MoE layer, H=2048, I=768,
+E=128, top-8, T=1 token, weights fp32 N(0, 0.02^2) quantised to Q4_0 (fp16
+block scales, 8 nibbles per uint32), bf16 N(0,1) activations, routing from
+N(0,1) logits through the engine's softmax-top-8 router.  A step is one
+fused-MoE layer forward.  The steps cycle over `--sets` independent weight
+sets (layers) and per-step routings, so the bytes streamed between two uses
+of a weight set exceed 2x the 126 MB L2 (inputs larger than L2).
+
+metric: effective weight bandwidth = unique active experts x bytes/expert
+        / time (test/benchmark_fused_moe_cpu.py:78-99,198 of the reference).
+
+Arms:
+  default            this engine (CUDA graphs of the torch.ops.nanovllm.moe_forward op)
+  --impl reference   the reference CPU engine (oracle/_ref, built unmodified from the
+                     reference sources) through its own torch.ops.nanovllm.moe_forward
+Multi-GPU (torchrun): experts are partitioned across ranks (expert parallel);
+each rank computes its experts' partial sum and one NCCL all-reduce combines.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E, K = 2048, 768, 128, 8
+Q4_BYTES_PER_EXPERT = (2 * I * H // 2) + (2 * I * (H // 32) * 2) + (H * I // 2) + (H * (I // 32) * 2)  # 2,654,208
+Q8_BYTES_PER_EXPERT = (2 * I * H) + (2 * I * (H // 32) * 2) + (H * I) + (H * (I // 32) * 2)  # 5,013,504
+METRIC = "fused MoE layer µs & effective weight GB/s vs HBM peak, tokens 1–4096, 1/2/4/8 GPU"
+HBM_FALLBACK = 6650.0
+# DRAM bytes (read + write) per launch of moe_decode_kernel<Q4> at this workload, from the
+# ncu capture summarised in profiles/moe_decode_q4_T1.md (None until captured).
+NCU_TRAFFIC_BYTES = None
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK, "fallback"
+
+
+# ----------------------------------------------------------------- weights
+def q4_quantize_torch(w):
+    """fp32 [..., N, Kd] -> (int32 packed [..., N, Kd/8], fp16 [..., N, Kd/32]); d = amax/7, RNE, clamp [-8,7]."""
+    import torch
+    shp = w.shape
+    b = w.reshape(*shp[:-1], shp[-1] // 32, 32)
+    d32 = b.abs().amax(-1) / 7.0
+    idv = torch.where(d32 != 0, 1.0 / d32, torch.zeros_like(d32))
+    q = torch.clamp(torch.round(b * idv.unsqueeze(-1)), -8, 7).to(torch.int64) + 8
+    q = q.reshape(*shp[:-1], shp[-1] // 8, 8)
+    shifts = torch.arange(0, 32, 4, device=w.device, dtype=torch.int64)
+    words = (q << shifts).sum(-1)
+    words = torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
+    return words, d32.to(torch.float16)
+
+
+def make_q4_layer(seed, device, e_lo=0, e_hi=E):
+    """One layer's Q4_0 weights for experts [e_lo, e_hi) (full-E tensors, other experts zero)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    gu_qs = torch.zeros((E, 2 * I, H // 8), dtype=torch.int32, device=device)
+    gu_d = torch.zeros((E, 2 * I, H // 32), dtype=torch.float16, device=device)
+    dn_qs = torch.zeros((E, H, I // 8), dtype=torch.int32, device=device)
+    dn_d = torch.zeros((E, H, I // 32), dtype=torch.float16, device=device)
+    for e0 in range(0, E, 16):
+        e1 = min(E, e0 + 16)
+        wg = torch.randn((e1 - e0, 2 * I, H), generator=g, device=device) * 0.02
+        wd = torch.randn((e1 - e0, H, I), generator=g, device=device) * 0.02
+        if e1 <= e_lo or e0 >= e_hi:
+            continue
+        a, b = q4_quantize_torch(wg)
+        gu_qs[e0:e1], gu_d[e0:e1] = a, b
+        a, b = q4_quantize_torch(wd)
+        dn_qs[e0:e1], dn_d[e0:e1] = a, b
+        del wg, wd
+    return gu_qs, gu_d, dn_qs, dn_d
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, out_path, gpu_index=0):
+        self.path = out_path
+        self.proc = None
+        self.gpu = gpu_index
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        try:
+            rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.strip()]
+            sm = [float(r[1]) for r in rows]
+            mx = float(rows[0][2])
+            reasons = set()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for r in rows:
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            loaded = [s for s in sm if s > 0.5 * mx] or sm
+            return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                    "samples": len(sm)}
+        except Exception as ex:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": str(ex)[:80]}
+
+
+# ----------------------------------------------------------------- cpu baseline (reference)
+def cpu_reference_worker(seconds: float, T: int):
+    """Runs in a subprocess: the reference engine (oracle/_ref) at this workload on the host cores."""
+    os.environ["NANOVLLM_TP_SIZE"] = "1"
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    gq = rng.integers(0, 2 ** 32, size=(E, 2 * I, H // 8), dtype=np.uint32).view(np.int32)
+    dq = rng.integers(0, 2 ** 32, size=(E, H, I // 8), dtype=np.uint32).view(np.int32)
+    gd = O.f32_to_f16_bits((rng.random((E, 2 * I, H // 32), dtype=np.float32) * 0.004).astype(np.float32))
+    dd = O.f32_to_f16_bits((rng.random((E, H, I // 32), dtype=np.float32) * 0.004).astype(np.float32))
+    eng = O.RefEngine(E, H, I, 1)
+    eng.store_repack(False, gq, gd, dq, dd)
+    times, nbytes = [], []
+    t_end = time.time() + seconds
+    i = 0
+    while time.time() < t_end or i < 3:
+        xb = O.f32_to_bf16_bits(rng.standard_normal((T, H), dtype=np.float32))
+        ids, w = O.topk_softmax(rng.standard_normal((T, E), dtype=np.float32), K, True)
+        eng.forward(xb, ids, w)
+        if i >= 2:
+            times.append(eng.last_ms())
+            nbytes.append(len(np.unique(ids)) * Q4_BYTES_PER_EXPERT)
+        i += 1
+    ms = statistics.mean(times)
+    print(json.dumps({"ms": ms, "gbs": statistics.mean(nbytes) / (ms * 1e-3) / 1e9, "calls": len(times),
+                      "cores": os.cpu_count()}))
+    sys.stdout.flush()
+    os._exit(0)
+
+
+def cpu_baseline(T: int, seconds: float = 12.0):
+    if not os.path.exists(os.path.join(ROOT, "oracle", "_ref", "ref_bridge.so")):
+        return None
+    try:
+        out = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-worker", str(seconds), "--tokens", str(T)],
+                             capture_output=True, text=True, timeout=seconds + 240,
+                             env={**os.environ, "NANOVLLM_TP_SIZE": "1"})
+        r = json.loads(out.stdout.strip().splitlines()[-1])
+    except Exception as ex:
+        return {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
+                "sample": f"failed: {str(ex)[:100]}"}
+    return {"value": round(r["gbs"], 3), "unit": "GB/s", "cores": r["cores"], "kind": "reference",
+            "ms_per_step": round(r["ms"], 4),
+            "sample": f"{r['calls']} T={T} Q4_0 forwards of the reference engine (scalar-NEON-shim build, tp=1, "
+                      f"NumaThreadPool on all {r['cores']} host threads), random routing, ~{seconds:.0f} s"}
+
+
+# ----------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    T = args.tokens
+    os.environ["NANOVLLM_TP_SIZE"] = "1"
+    os.environ.setdefault("NANOVLLM_TP_THREADS_PER_NODE", str(os.cpu_count()))
+    so = os.path.join(ROOT, "oracle", "_ref", "nanovllm_ext_ref.so")
+    if not os.path.exists(so):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/nanovllm_ext_ref.so not built "
+                          "(needs the reference checkout; run oracle/Makefile ref)"}))
+        return 0
+    import ctypes
+    import torch
+    torch.ops.load_library(so)
+    ctypes.CDLL(so).ref_pool_warmup()  # closes the reference pool's start-up race (oracle/ref_warmup.cpp)
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    handles = []
+    nsets = 2
+    for s in range(nsets):
+        h = torch.classes.nanovllm.MoEInfer(E, H, I, 1)
+        gq = torch.from_numpy(rng.integers(0, 2 ** 32, size=(E, 2 * I, H // 8), dtype=np.uint32).view(np.int32))
+        dq = torch.from_numpy(rng.integers(0, 2 ** 32, size=(E, H, I // 8), dtype=np.uint32).view(np.int32))
+        gd = (torch.rand((E, 2 * I, H // 32)) * 0.004).to(torch.float16)
+        dd = (torch.rand((E, H, I // 32)) * 0.004).to(torch.float16)
+        h.store_quantized_repack(gq, gd, dq, dd)
+        handles.append(h)
+    steps = []
+    for i in range(64):
+        x = torch.randn(T, H).to(torch.bfloat16)
+        ids, w = O.topk_softmax(rng.standard_normal((T, E), dtype=np.float32), K, True)
+        steps.append((x, torch.from_numpy(ids), torch.from_numpy(w), len(np.unique(ids)) * Q4_BYTES_PER_EXPERT))
+    for i in range(args.warmup):
+        x, ids, w, _ = steps[i % len(steps)]
+        torch.ops.nanovllm.moe_forward(x, ids, w, handles[i % nsets])
+    t0 = time.perf_counter()
+    tot_b = 0
+    for i in range(args.steps):
+        x, ids, w, nb = steps[i % len(steps)]
+        torch.ops.nanovllm.moe_forward(x, ids, w, handles[i % nsets])
+        tot_b += nb
+    dt = time.perf_counter() - t0
+    ms = dt / args.steps * 1e3
+    val = tot_b / dt / 1e9
+    line = {"metric": METRIC, "value": round(val, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"Q4_0 fused MoE layer H{H} I{I} E{E} top{K} T={T} (BASELINE configs[1])",
+                       "tokens": T},
+            "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
+                             "sample": f"{args.steps} T={T} forwards via torch.ops.nanovllm.moe_forward of the "
+                                       f"reference built unmodified (scalar NEON shim, tp=1, {os.cpu_count()} threads)"},
+            "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    sys.stdout.flush()
+    os._exit(0)
+
+
+# ----------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    import moe_ascend_opt_b200  # noqa: F401
+
+    T = args.tokens
+    nsets = args.sets
+    el = E // world
+    e_lo, e_hi = rank * el, (rank + 1) * el
+    handles = []
+    for s in range(nsets):
+        h = torch.classes.nanovllm.MoEInfer(E, H, I, 1)
+        if world > 1:
+            h.set_expert_parallel(rank, world)
+        ws = make_q4_layer(1000 + s, dev, e_lo, e_hi)
+        h.store_quantized_repack(*ws)
+        del ws
+        h.reserve(max(T, 32), K)
+        handles.append(h)
+    torch.cuda.synchronize()
+
+    # per-step inputs: hidden + routing through the engine's router
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    nin = max(nsets, 16)
+    xs, idss, wss, nbytes = [], [], [], []
+    for i in range(nin):
+        x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+        logits = torch.randn((T, E), generator=g, device=dev)
+        ids, w = torch.ops.nanovllm.moe_route(logits, K, True)
+        xs.append(x); idss.append(ids); wss.append(w)
+        nbytes.append(int(torch.unique(ids).numel()) * Q4_BYTES_PER_EXPERT)
+    combine_out = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(nin)]
+
+    def step(i):
+        h = handles[i % nsets]
+        j = i % nin
+        if world == 1:
+            return torch.ops.nanovllm.moe_forward(xs[j], idss[j], wss[j], h)
+        part = torch.ops.nanovllm.moe_forward_partial(xs[j], idss[j], wss[j], h)
+        dist.all_reduce(part)
+        combine_out[j].copy_(part)
+        return combine_out[j]
+
+    # CUDA graphs (1 GPU): one graph per (set, input) pair in the cycle
+    graphs = None
+    ncycle = int(np.lcm(nsets, nin))
+    if world == 1 and not args.no_graph:
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for i in range(3):
+                    step(i)
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            graphs = []
+            for i in range(ncycle):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    step(i)
+                graphs.append(gr)
+            torch.cuda.synchronize()
+        except Exception as ex:  # eager launches are equally valid, just slower on the host
+            print(f"[bench] graph capture unavailable ({str(ex)[:80]}); eager launches", file=sys.stderr)
+            graphs = None
+
+    def run(i):
+        if graphs is not None:
+            graphs[i % ncycle].replay()
+        else:
+            step(i)
+
+    for i in range(args.warmup):
+        run(i)
+    torch.cuda.synchronize()
+
+    def timed(nsteps, offset=0):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(nsteps):
+            run(offset + i)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    outdir = os.path.join(ROOT, "gpurun_out")
+    clk = ClockSampler(os.path.join(outdir if os.path.isdir(outdir) else "/tmp", f"clocks_rank{rank}.csv"), local)
+    with clk:
+        # soak so the clock record covers a loaded GPU, then the timed region
+        t_soak = time.time()
+        while time.time() - t_soak < 1.0:
+            timed(min(args.steps, 2000))
+        total_ms = timed(args.steps)
+    clocks = clk.summary()
+
+    avg_bytes = sum(nbytes[i % nin] for i in range(args.steps)) / args.steps
+    ms_step = total_ms / args.steps
+    value = avg_bytes / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+
+    out = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "us_per_layer": round(ms_step * 1e3, 3),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+           "data": "synthetic",
+           "config": {"workload": f"Q4_0 fused MoE layer H{H} I{I} E{E} top{K} T={T} (BASELINE configs[1])",
+                      "tokens": T, "weight_sets": nsets,
+                      "l2": f"inputs larger than L2: {nsets} rotating weight sets x {E} experts "
+                            f"({nsets * E * Q4_BYTES_PER_EXPERT / 1e9:.1f} GB) and {nin} rotating routings",
+                      "parallelism": f"ep{world}" if world > 1 else "single",
+                      "launch": "cuda_graph" if graphs is not None else "eager",
+                      "avg_active_experts": round(avg_bytes / Q4_BYTES_PER_EXPERT, 2)},
+           "gpu_launches": args.steps * (1 if world == 1 else 1),
+           "clocks": clocks}
+    if world == 1:
+        out["roofline"] = {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
+                           "frac": round(value / peak, 4), "peak_source": peak_kind,
+                           "traffic": NCU_TRAFFIC_BYTES,
+                           "algorithmic_bytes_per_launch": round(avg_bytes),
+                           "kernel": "moe_decode_kernel<Q4_0>"}
+    # end-to-end through the public op with host buffers and copies in the timed region
+    if rank == 0 or world > 1:
+        xh = [x.cpu().pin_memory() for x in xs]
+        ih = [i.cpu().pin_memory() for i in idss]
+        wh = [w.cpu().pin_memory() for w in wss]
+        yh = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+        xd = torch.empty_like(xs[0]); idd = torch.empty_like(idss[0]); wd = torch.empty_like(wss[0])
+        n_e2e = min(args.steps, 2000)
+
+        def e2e_step(i):
+            j = i % nin
+            xd.copy_(xh[j], non_blocking=True)
+            idd.copy_(ih[j], non_blocking=True)
+            wd.copy_(wh[j], non_blocking=True)
+            h = handles[i % nsets]
+            if world == 1:
+                y = torch.ops.nanovllm.moe_forward(xd, idd, wd, h)
+            else:
+                y = torch.ops.nanovllm.moe_forward_partial(xd, idd, wd, h)
+                dist.all_reduce(y)
+                y = y.to(torch.bfloat16)
+            yh.copy_(y, non_blocking=True)
+
+        for i in range(3):
+            e2e_step(i)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n_e2e):
+            e2e_step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        eb = sum(nbytes[i % nin] for i in range(n_e2e)) / n_e2e
+        out["e2e"] = {"value": round(eb / (ems / n_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                      "ms_per_step": round(ems / n_e2e, 6), "steps": n_e2e,
+                      "h2d_bytes_per_step": T * H * 2 + T * K * 8, "d2h_bytes_per_step": T * H * 2,
+                      "api": "torch.ops.nanovllm.moe_forward (eager, pinned host buffers)"}
+    if world == 1 and not args.no_cpu:
+        out["cpu_baseline"] = cpu_baseline(T)
+    if args.sweep and world == 1:
+        out["sweep"] = sweep(handles, dev, args)
+    if rank == 0:
+        print(json.dumps(out))
+        sys.stdout.flush()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def sweep(handles, dev, args):
+    """Eager per-T timing (events) for the token sweep of BASELINE configs[1]."""
+    import torch
+    res = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    for T in (1, 4, 8, 32):
+        xs, ids_l, w_l, nb = [], [], [], []
+        for i in range(16):
+            xs.append(torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16))
+            ids, w = torch.ops.nanovllm.moe_route(torch.randn((T, E), generator=g, device=dev), K, True)
+            ids_l.append(ids); w_l.append(w); nb.append(int(torch.unique(ids).numel()) * Q4_BYTES_PER_EXPERT)
+        n = 200
+        for i in range(5):
+            torch.ops.nanovllm.moe_forward(xs[i % 16], ids_l[i % 16], w_l[i % 16], handles[i % len(handles)])
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n):
+            torch.ops.nanovllm.moe_forward(xs[i % 16], ids_l[i % 16], w_l[i % 16], handles[i % len(handles)])
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        b = sum(nb[i % 16] for i in range(n)) / n
+        res[f"T{T}"] = {"us": round(ms * 1e3, 2), "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
+                        "active_experts": round(b / Q4_BYTES_PER_EXPERT, 1)}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--sets", type=int, default=16)
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--cpu-worker", type=float, default=None)
+    args = ap.parse_args()
+    if args.cpu_worker is not None:
+        return cpu_reference_worker(args.cpu_worker, args.tokens)
+    if args.impl == "reference":
+        args.steps = min(args.steps, 5000)  # each reference step is a ms-scale CPU forward
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -595,7 +595,10 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     while (slice > 0 && !plan_decode(eng, (int)slice, (int)K, pl)) slice = slice > 8 ? slice / 2 : slice - 1;
     if (slice == 0) return fail(MOE_ERR_INVALID, "shapes exceed the decode kernel's shared memory");
     if (int rc = ensure_workspace(eng, slice * K)) return rc;
-    CUDA_TRY(cudaEventRecord(eng->ev0, st));
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    CUDA_TRY(cudaStreamIsCapturing(st, &cap));
+    const bool timed = cap == cudaStreamCaptureStatusNone;
+    if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
     for (int64_t t0 = 0; t0 < T; t0 += slice) {
         const int64_t n = std::min(slice, T - t0);
         if (n != slice && !plan_decode(eng, (int)n, (int)K, pl)) return fail(MOE_ERR_INVALID, "plan failed");
@@ -612,8 +615,10 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         const int rc = eng->cfg.quant_type == MOE_Q4_0 ? launch_decode<true>(pl, st) : launch_decode<false>(pl, st);
         if (rc) return rc;
     }
-    CUDA_TRY(cudaEventRecord(eng->ev1, st));
-    eng->timed = true;
+    if (timed) {
+        CUDA_TRY(cudaEventRecord(eng->ev1, st));
+        eng->timed = true;
+    }
     return MOE_OK;
 }
 
