@@ -357,7 +357,7 @@ def run_ours(args):
     with clk:
         # soak so the clock record covers a loaded GPU, then the timed region
         t_soak = time.time()
-        while time.time() - t_soak < 1.0:
+        while not args.no_soak and time.time() - t_soak < 1.0:
             timed(min(args.steps, 2000))
         total_ms = timed(args.steps)
     clocks = clk.summary()
@@ -485,6 +485,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock soak (profiling runs)")
     ap.add_argument("--cpu-worker", type=float, default=None)
     args = ap.parse_args()
     if args.cpu_worker is not None:
