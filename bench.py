@@ -300,8 +300,10 @@ def run_ours(args):
         combine_out[j].copy_(part)
         return combine_out[j]
 
-    # CUDA graphs (1 GPU): one graph per (set, input) pair in the cycle
+    # CUDA graphs (1 GPU): one graph holding a whole cycle of `ncycle` layer steps (a layer
+    # stack, so the host launches once per cycle), plus one graph per step for remainders.
     graphs = None
+    cycle_graph = None
     ncycle = int(np.lcm(nsets, nin))
     if world == 1 and not args.no_graph:
         try:
@@ -318,16 +320,33 @@ def run_ours(args):
                 with torch.cuda.graph(gr):
                     step(i)
                 graphs.append(gr)
+            cycle_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cycle_graph):
+                for i in range(ncycle):
+                    step(i)
             torch.cuda.synchronize()
         except Exception as ex:  # eager launches are equally valid, just slower on the host
             print(f"[bench] graph capture unavailable ({str(ex)[:80]}); eager launches", file=sys.stderr)
             graphs = None
+            cycle_graph = None
 
     def run(i):
         if graphs is not None:
             graphs[i % ncycle].replay()
         else:
             step(i)
+
+    def run_steps(offset, nsteps):
+        """Exactly `nsteps` layer steps starting at step `offset`."""
+        i = offset
+        end = offset + nsteps
+        if cycle_graph is not None:
+            while i < end and i % ncycle != 0:
+                run(i); i += 1
+            while end - i >= ncycle:
+                cycle_graph.replay(); i += ncycle
+        while i < end:
+            run(i); i += 1
 
     for i in range(args.warmup):
         run(i)
@@ -341,8 +360,7 @@ def run_ours(args):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        for i in range(nsteps):
-            run(offset + i)
+        run_steps(offset, nsteps)
         e1.record(st)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
@@ -376,7 +394,8 @@ def run_ours(args):
                       "l2": f"inputs larger than L2: {nsets} rotating weight sets x {E} experts "
                             f"({nsets * E * Q4_BYTES_PER_EXPERT / 1e9:.1f} GB) and {nin} rotating routings",
                       "parallelism": f"ep{world}" if world > 1 else "single",
-                      "launch": "cuda_graph" if graphs is not None else "eager",
+                      "launch": (f"cuda_graph ({ncycle} layer steps per graph replay)" if cycle_graph is not None
+                                 else "eager"),
                       "avg_active_experts": round(avg_bytes / Q4_BYTES_PER_EXPERT, 2)},
            "gpu_launches": args.steps * (1 if world == 1 else 1),
            "clocks": clocks}

@@ -128,6 +128,15 @@ int moe_route_permute(const int32_t* topk_ids, int64_t num_tokens, int64_t top_k
 int moe_quantize_rows_q8_0(const void* x, int32_t dtype, int64_t rows, int64_t cols, int8_t* qs,
                            float* d, void* stream);
 
+/* Diagnostics (no counterpart in the reference): enable != 0 makes every later decode
+ * launch record 16 globaltimer stamps (ns) per CTA (phase boundaries of the fused kernel:
+ * start, routing, activation quantisation, first/last gate_up data, gate_up done, grid
+ * barrier entered/passed, h requantised, first down data, down done, combine done);
+ * enable == 0 turns it off.  When `out` is non-null, copies up to max_entries stamps of
+ * the last launch (waits for the device).  *n_entries = CTAs x 16 while enabled. */
+int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64_t* out, int32_t max_entries,
+                              int32_t* n_entries);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* moe_last_error(void);
 

@@ -21,7 +21,7 @@ SYMBOLS = [
     "moe_engine_create", "moe_engine_destroy", "moe_engine_load_quantized", "moe_engine_quantize_store_expert",
     "moe_engine_load_awq", "moe_engine_forward", "moe_engine_reserve", "moe_engine_last_time_ms",
     "moe_engine_device_error", "moe_engine_export_expert", "moe_route_topk", "moe_route_permute",
-    "moe_quantize_rows_q8_0", "moe_last_error",
+    "moe_quantize_rows_q8_0", "moe_engine_debug_timeline", "moe_last_error",
 ]
 
 
@@ -64,6 +64,7 @@ def lib() -> C.CDLL:
             "moe_route_topk": [_P, _I64, _I64, _I64, _I32, _P, _P, _P],
             "moe_route_permute": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P],
             "moe_quantize_rows_q8_0": [_P, _I32, _I64, _I64, _P, _P, _P],
+            "moe_engine_debug_timeline": [_P, _I32, _P, _I32, C.POINTER(_I32)],
         }
         for name, args in sig.items():
             f = getattr(L, name)
@@ -130,6 +131,18 @@ class Engine:
 
     def export_expert(self, e, which, qs_out, d_out):
         call("moe_engine_export_expert", self.h, e, which, qs_out.ctypes.data, d_out.ctypes.data)
+
+    def timeline(self, enable=None):
+        """Enable/disable per-CTA phase stamps, or (enable=None) fetch the last launch's [CTAs, 16] ns stamps."""
+        import numpy as np
+        n = C.c_int32()
+        if enable is not None:
+            call("moe_engine_debug_timeline", self.h, int(enable), None, 0, C.byref(n))
+            return None
+        call("moe_engine_debug_timeline", self.h, 1, None, 0, C.byref(n))
+        out = np.zeros(n.value, np.uint64)
+        call("moe_engine_debug_timeline", self.h, 1, out.ctypes.data, n.value, C.byref(n))
+        return out.reshape(-1, 16)
 
     def close(self):
         if self.h:

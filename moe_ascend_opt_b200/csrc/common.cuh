@@ -58,7 +58,8 @@ MOE_DEV float silu_mul(float g, float up) {
 // One Q8_0 block scale as the reference binary computes it: d = amax * (1/127)
 // (Int8-gemm/gemm_kernels.cpp:43 under -ffast-math), id = d ? 1/d : 0.
 MOE_DEV float q8_scale(float amax) { return __fmul_rn(amax, 1.0f / 127.0f); }
-MOE_DEV float q8_inv(float d) { return d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f; }
+// __frcp_rn is the correctly rounded reciprocal, i.e. the IEEE quotient 1/d.
+MOE_DEV float q8_inv(float d) { return d != 0.0f ? __frcp_rn(d) : 0.0f; }
 MOE_DEV int q8_quant(float v, float id) {
     int q = __float2int_rn(__fmul_rn(v, id));  // round to nearest even
     return q > 127 ? 127 : (q < -128 ? -128 : q);
@@ -129,25 +130,38 @@ MOE_DEV uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
-// Sense-reversing grid barrier over `nblocks` co-resident CTAs (cooperative launch).
-// bar[0] = arrival count, bar[1] = generation.  Called by one thread per CTA.
-// Returns false (and sets *err) when the wait budget ran out.
-MOE_DEV bool grid_barrier(uint32_t* bar, uint32_t nblocks, int32_t* err) {
-    const uint32_t gen = ld_acquire_gpu(bar + 1);
-    __threadfence();
-    const uint32_t old = atomicAdd(bar, 1u);
-    if (old == nblocks - 1) {
-        atomicExch(bar, 0u);
-        __threadfence();
-        atomicAdd(bar + 1, 1u);
-        return true;
-    }
+MOE_DEV unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+MOE_DEV unsigned long long atom_add_release_gpu_u64(unsigned long long* p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+
+// Grid barrier over `nblocks` co-resident CTAs (cooperative launch), one thread
+// per CTA.  `ctr` counts arrivals monotonically over all launches; launch n
+// (0-based, read by barrier_launch_index at its start) is released once the
+// counter reaches (n+1)*nblocks.  The arrival is a fire-and-forget release
+// reduction (orders this CTA's earlier global writes before it), then acquire
+// polling.  Returns false (and sets *err) when the wait budget ran out.
+MOE_DEV bool grid_barrier(unsigned long long* ctr, uint32_t nblocks, unsigned long long target, int32_t* err) {
+    (void)nblocks;
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(ctr), "l"(1ull) : "memory");
     for (uint32_t it = 0; it < kSpinLimit; ++it) {
-        if (ld_acquire_gpu(bar + 1) != gen) return true;
-        __nanosleep(it < 256 ? 20 : 256);
+        if (ld_acquire_gpu_u64(ctr) >= target) return true;
+        if (it > 4096) __nanosleep(256);  // hot spin first: the barrier is on the critical path
     }
     atomicExch(reinterpret_cast<int*>(err), kErrGridBarrier);
     return false;
+}
+
+// Index of the current launch on this barrier counter (valid before this CTA arrives).
+MOE_DEV unsigned long long barrier_launch_index(const unsigned long long* ctr, uint32_t nblocks) {
+    return ld_acquire_gpu_u64(ctr) / nblocks;
 }
 
 }  // namespace moe

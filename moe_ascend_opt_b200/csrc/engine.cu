@@ -43,20 +43,25 @@ struct moe_engine {
     bool loaded = false;
     int scale_bf16 = 0;
     // Q8_0 / Q4_0 device layout
-    uint8_t* gu_qs = nullptr;  // [E][I][2][rs1]
-    uint8_t* gu_sc = nullptr;  // [E][I][2][ss1]
-    uint8_t* dn_qs = nullptr;  // [E][H][rs2]
-    uint8_t* dn_sc = nullptr;  // [E][H][ss2]
+    // gate_up unit records [E][I]: gate qs row j | up qs row j | gate scales | up scales
+    uint8_t* gu = nullptr;
+    // down row records [E][H]: qs row | scales
+    uint8_t* dn = nullptr;
     int rs1 = 0, ss1 = 0, rs2 = 0, ss2 = 0;
+    int64_t unit_bytes() const { return 2 * (int64_t)(rs1 + ss1); }
+    int64_t row_bytes() const { return (int64_t)(rs2 + ss2); }
     // AWQ device layout
     AwqWeights awq{};
     // workspace
     float* h_ws = nullptr;
     int64_t h_cap = 0;  // positions
+    uint32_t* hmax = nullptr;  // [2][h_cap * I/32]
     uint32_t* bar = nullptr;
     int32_t* err = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     bool timed = false;
+    unsigned long long* timeline = nullptr;  // per-CTA phase stamps when enabled
+    int timeline_ctas = 0;
 };
 
 namespace {
@@ -74,42 +79,47 @@ struct DeviceGuard {
     }
 };
 
-// Copy rows with a row map: dst row d <- src row map(d), `bytes` per row,
-// destination rows padded with zeros to `dstride`.
-enum RowMap { kIdentity = 0, kGateUpInterleave = 1 };
+// Load-time packing: copy `bytes` of every source row into its record.
+// kGateUp: source row e*2I + r*I + j (r = 0 gate, 1 up) -> record (e*I + j) at
+//          offset base + r*part; kDown: source row e*H + n -> record (e*H + n) at base.
+enum RowMap { kDown = 0, kGateUp = 1 };
 
-__global__ void pack_rows_kernel(uint8_t* dst, const uint8_t* src, int64_t nrows, int64_t bytes,
-                                 int64_t dstride, int64_t sstride, int map, int64_t I) {
-    const int64_t row = blockIdx.x;
-    if (row >= nrows) return;
-    int64_t srow = row;
-    if (map == kGateUpInterleave) {  // dst row = (e*I + j)*2 + r ; src row = e*2I + r*I + j
-        const int64_t r = row & 1, ej = row >> 1, e = ej / I, j = ej % I;
-        srow = e * 2 * I + r * I + j;
+MOE_DEV int64_t record_of(int map, int64_t srow, int64_t I, int64_t* r) {
+    if (map == kGateUp) {
+        const int64_t e = srow / (2 * I), rem = srow % (2 * I);
+        *r = rem / I;
+        return e * I + rem % I;
     }
-    const uint8_t* s = src + srow * sstride;
-    uint8_t* d = dst + row * dstride;
-    for (int64_t c = threadIdx.x; c < dstride; c += blockDim.x) d[c] = c < bytes ? s[c] : 0;
+    *r = 0;
+    return srow;
 }
 
-// Inverse of pack_rows_kernel for one expert (export / bit-exact decode check).
-__global__ void unpack_rows_kernel(uint8_t* dst, const uint8_t* src, int64_t nrows, int64_t bytes,
-                                   int64_t sstride, int map, int64_t I) {
-    const int64_t srow = blockIdx.x;  // row in the packed (destination-layout) buffer
+__global__ void pack_rows_kernel(uint8_t* dst, const uint8_t* src, int64_t nrows, int64_t bytes, int64_t rec_bytes,
+                                 int64_t base, int64_t part, int map, int64_t I) {
+    const int64_t srow = blockIdx.x;
     if (srow >= nrows) return;
-    int64_t drow = srow;
-    if (map == kGateUpInterleave) {
-        const int64_t r = srow & 1, j = srow >> 1;
-        drow = r * I + j;
-    }
-    for (int64_t c = threadIdx.x; c < bytes; c += blockDim.x) dst[drow * bytes + c] = src[srow * sstride + c];
+    int64_t r;
+    const int64_t rec = record_of(map, srow, I, &r);
+    uint8_t* d = dst + rec * rec_bytes + base + r * part;
+    const uint8_t* s = src + srow * bytes;
+    for (int64_t c = threadIdx.x; c < bytes; c += blockDim.x) d[c] = s[c];
+}
+
+// Inverse of pack_rows_kernel (export / bit-exact decode check): record fields -> source rows.
+__global__ void unpack_rows_kernel(uint8_t* dst, const uint8_t* src, int64_t nrows, int64_t bytes, int64_t rec_bytes,
+                                   int64_t base, int64_t part, int map, int64_t I) {
+    const int64_t srow = blockIdx.x;
+    if (srow >= nrows) return;
+    int64_t r;
+    const int64_t rec = record_of(map, srow, I, &r);
+    const uint8_t* s = src + rec * rec_bytes + base + r * part;
+    for (int64_t c = threadIdx.x; c < bytes; c += blockDim.x) dst[srow * bytes + c] = s[c];
 }
 
 // Online Q8_0 quantisation of one weight matrix [rows, cols] straight into the
 // device layout (quantize_weight_only, Int8-gemm/q8_gemm.cpp:197-260: fp16 scale).
 __global__ void quantize_weight_rows_kernel(const void* w, int w_dtype, int64_t rows, int64_t cols,
-                                            uint8_t* qs_base, int64_t qs_row_stride, int64_t qs_row_step,
-                                            uint8_t* sc_base, int64_t sc_row_stride, int64_t sc_row_step) {
+                                            uint8_t* qs_base, uint8_t* sc_base, int64_t row_stride) {
     // one warp per 32-block; lane = element
     const int lane = threadIdx.x & 31;
     const int64_t nb = cols / 32;
@@ -125,10 +135,10 @@ __global__ void quantize_weight_rows_kernel(const void* w, int w_dtype, int64_t 
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float d = q8_scale(amax);
     const float id = q8_inv(d);
-    uint8_t* qrow = qs_base + r * qs_row_step * qs_row_stride;
+    uint8_t* qrow = qs_base + r * row_stride;
     qrow[b * 32 + lane] = (uint8_t)(int8_t)q8_quant(v, id);
     if (lane == 0) {
-        uint16_t* srow = reinterpret_cast<uint16_t*>(sc_base + r * sc_row_step * sc_row_stride);
+        uint16_t* srow = reinterpret_cast<uint16_t*>(sc_base + r * row_stride);
         srow[b] = __half_as_ushort(__float2half_rn(d));
     }
 }
@@ -292,15 +302,11 @@ int alloc_q_layout(moe_engine* eng) {
     eng->ss1 = (int)round_up((H / 32) * 2, 16);
     eng->rs2 = (int)round_up(q4 ? I / 2 : I, 16);
     eng->ss2 = (int)round_up((I / 32) * 2, 16);
-    if (!eng->gu_qs) {
-        CUDA_TRY(cudaMalloc(&eng->gu_qs, (size_t)E * I * 2 * eng->rs1));
-        CUDA_TRY(cudaMalloc(&eng->gu_sc, (size_t)E * I * 2 * eng->ss1));
-        CUDA_TRY(cudaMalloc(&eng->dn_qs, (size_t)E * H * eng->rs2));
-        CUDA_TRY(cudaMalloc(&eng->dn_sc, (size_t)E * H * eng->ss2));
-        CUDA_TRY(cudaMemset(eng->gu_qs, 0, (size_t)E * I * 2 * eng->rs1));
-        CUDA_TRY(cudaMemset(eng->gu_sc, 0, (size_t)E * I * 2 * eng->ss1));
-        CUDA_TRY(cudaMemset(eng->dn_qs, 0, (size_t)E * H * eng->rs2));
-        CUDA_TRY(cudaMemset(eng->dn_sc, 0, (size_t)E * H * eng->ss2));
+    if (!eng->gu) {
+        CUDA_TRY(cudaMalloc(&eng->gu, (size_t)E * I * eng->unit_bytes()));
+        CUDA_TRY(cudaMalloc(&eng->dn, (size_t)E * H * eng->row_bytes()));
+        CUDA_TRY(cudaMemset(eng->gu, 0, (size_t)E * I * eng->unit_bytes()));
+        CUDA_TRY(cudaMemset(eng->dn, 0, (size_t)E * H * eng->row_bytes()));
     }
     return MOE_OK;
 }
@@ -314,9 +320,15 @@ int ensure_workspace(moe_engine* eng, int64_t positions) {
     if (positions <= eng->h_cap) return MOE_OK;
     int64_t cap = eng->h_cap ? eng->h_cap : 64;
     while (cap < positions) cap *= 2;
+    CUDA_TRY(cudaDeviceSynchronize());  // the old buffers may still be in use by queued work
     if (eng->h_ws) CUDA_TRY(cudaFree(eng->h_ws));
+    if (eng->hmax) CUDA_TRY(cudaFree(eng->hmax));
     eng->h_ws = nullptr;
+    eng->hmax = nullptr;
+    const size_t hm = (size_t)cap * (eng->cfg.intermediate_size / 32);
     CUDA_TRY(cudaMalloc(&eng->h_ws, (size_t)cap * eng->cfg.intermediate_size * sizeof(float)));
+    CUDA_TRY(cudaMalloc(&eng->hmax, 2 * hm * sizeof(uint32_t)));
+    CUDA_TRY(cudaMemset(eng->hmax, 0, 2 * hm * sizeof(uint32_t)));
     eng->h_cap = cap;
     return MOE_OK;
 }
@@ -334,6 +346,10 @@ bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
     const int G = eng->num_sms;
     DecodeParams& p = pl.p;
     std::memset(&p, 0, sizeof(p));
+    int lpr = 4;  // phase 2: 4 lanes per down row, 8 rows per item
+    while (lpr > 1 && nb2 % lpr != 0) lpr >>= 1;
+    p.lanes_per_row = lpr;
+    const int rpg = 32 / lpr;
     int64_t off = round_up((int64_t)(3 * TK + 5 * E + 4) * 4, 128);
     p.off_x = (int)off;
     const int64_t xbytes = round_up((int64_t)T * H, 16) + (int64_t)T * nb1 * 8;
@@ -342,25 +358,23 @@ bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
     p.off_out = (int)off;
     p.rows_max = (H + G - 1) / G;
     off += round_up((int64_t)TK * p.rows_max * 4, 128);
-    const int64_t unit_bytes = 2 * (int64_t)(eng->rs1 + eng->ss1);
-    const int64_t row2_bytes = (int64_t)p.rows_max * (eng->rs2 + eng->ss2);
-    int64_t stage = std::max<int64_t>(32768, std::max(unit_bytes, row2_bytes));
-    stage = round_up(stage, 128);
-    const int64_t avail = (int64_t)eng->max_smem - off - 128;  // room for mbarriers
-    int ns = (int)std::min<int64_t>(8, avail / (stage + 16));
-    if (ns < 2) return false;
-    p.nstages = ns;
-    p.stage_bytes = (int)stage;
-    off = round_up(off + 16 * ns, 128);
-    p.off_stage = (int)off;
-    // barriers sit in the 16*ns bytes right before off_stage
-    off += (int64_t)ns * stage;
-    if (off > eng->max_smem) return false;
-    p.units_per_chunk = (int)std::max<int64_t>(1, stage / unit_bytes);
-    p.experts_per_chunk = (int)std::max<int64_t>(1, stage / std::max<int64_t>(1, row2_bytes));
-    int lpr = 32;
-    while (lpr > 1 && nb2 % lpr != 0) lpr >>= 1;
-    p.lanes_per_row = lpr;
+    const int64_t unit_bytes = eng->unit_bytes();
+    const int64_t item_bytes = (int64_t)rpg * eng->row_bytes();
+    const int64_t avail = (int64_t)eng->max_smem - off - 1024;  // mbarriers + static smem
+    const int64_t per_warp = avail / kWarps;
+    // phase-1 items of up to 4 units, at least 2 slots per warp
+    int upi = 4;
+    while (upi > 1 && 2 * round_up(std::max((int64_t)upi * unit_bytes, item_bytes), 128) > per_warp) upi >>= 1;
+    const int64_t slot = round_up(std::max((int64_t)upi * unit_bytes, item_bytes), 128);
+    int slots = (int)std::min<int64_t>(6, per_warp / slot);
+    if (slots < 2) return false;
+    p.units_per_item = upi;
+    p.slots = slots;
+    p.slot_bytes = (int)slot;
+    off = round_up(off + 8 * kWarps * slots, 128);
+    p.off_ring = (int)off;  // mbarriers sit in the 8*kWarps*slots bytes right before the ring
+    off += (int64_t)kWarps * slots * slot;
+    if (off > eng->max_smem - 256) return false;
     p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
     p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
     p.scale_bf16 = eng->scale_bf16;
@@ -381,7 +395,7 @@ int launch_decode(const DecodePlan& pl, cudaStream_t st) {
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(pl.grid);
-    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -440,13 +454,13 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
 extern "C" int moe_engine_destroy(moe_engine* eng) {
     if (!eng) return MOE_OK;
     DeviceGuard g(eng->cfg.device);
-    cudaFree(eng->gu_qs);
-    cudaFree(eng->gu_sc);
-    cudaFree(eng->dn_qs);
-    cudaFree(eng->dn_sc);
+    cudaFree(eng->gu);
+    cudaFree(eng->dn);
     awq_free(eng->awq);
     cudaFree(eng->h_ws);
+    cudaFree(eng->hmax);
     cudaFree(eng->bar);
+    cudaFree(eng->timeline);
     if (eng->ev0) cudaEventDestroy(eng->ev0);
     if (eng->ev1) cudaEventDestroy(eng->ev1);
     delete eng;
@@ -466,19 +480,20 @@ extern "C" int moe_engine_load_quantized(moe_engine* eng, const void* gu_qs, con
     const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
     const bool q4 = eng->cfg.quant_type == MOE_Q4_0;
     const int64_t gu_row = q4 ? H / 2 : H, dn_row = q4 ? I / 2 : I;
-    struct Piece { const void* src; size_t bytes; int64_t rows, row_bytes, dstride; uint8_t* dst; int map; };
+    struct Piece { const void* src; int64_t rows, row_bytes; uint8_t* dst; int64_t rec, base, part; int map; };
+    const int64_t U1 = eng->unit_bytes(), R2 = eng->row_bytes();
     Piece pieces[4] = {
-        {gu_qs, (size_t)E * 2 * I * gu_row, E * 2 * I, gu_row, eng->rs1, eng->gu_qs, kGateUpInterleave},
-        {gu_d, (size_t)E * 2 * I * (H / 32) * 2, E * 2 * I, (H / 32) * 2, eng->ss1, eng->gu_sc, kGateUpInterleave},
-        {dn_qs, (size_t)E * H * dn_row, E * H, dn_row, eng->rs2, eng->dn_qs, kIdentity},
-        {dn_d, (size_t)E * H * (I / 32) * 2, E * H, (I / 32) * 2, eng->ss2, eng->dn_sc, kIdentity},
+        {gu_qs, E * 2 * I, gu_row, eng->gu, U1, 0, eng->rs1, kGateUp},
+        {gu_d, E * 2 * I, (H / 32) * 2, eng->gu, U1, 2 * (int64_t)eng->rs1, eng->ss1, kGateUp},
+        {dn_qs, E * H, dn_row, eng->dn, R2, 0, 0, kDown},
+        {dn_d, E * H, (I / 32) * 2, eng->dn, R2, eng->rs2, 0, kDown},
     };
     for (auto& pc : pieces) {
         const uint8_t* src = nullptr;
         uint8_t* owned = nullptr;
-        if (int rc = stage_to_device(pc.src, pc.bytes, src_on_device, st, &src, &owned)) return rc;
-        pack_rows_kernel<<<(unsigned)pc.rows, 128, 0, st>>>(pc.dst, src, pc.rows, pc.row_bytes, pc.dstride,
-                                                             pc.row_bytes, pc.map, I);
+        if (int rc = stage_to_device(pc.src, (size_t)pc.rows * pc.row_bytes, src_on_device, st, &src, &owned)) return rc;
+        pack_rows_kernel<<<(unsigned)pc.rows, 128, 0, st>>>(pc.dst, src, pc.rows, pc.row_bytes, pc.rec, pc.base,
+                                                             pc.part, pc.map, I);
         CUDA_TRY(cudaGetLastError());
         if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
     }
@@ -508,19 +523,19 @@ extern "C" int moe_engine_quantize_store_expert(moe_engine* eng, int64_t expert,
     uint8_t* owned = nullptr;
     if (int rc = stage_to_device(w, (size_t)rows * cols * esz, src_on_device, st, &src, &owned)) return rc;
     uint8_t *qb, *sb;
-    int64_t qstride, sstride, step;
+    int64_t stride;
     if (proj == 2) {
-        qb = eng->dn_qs + (size_t)expert * H * eng->rs2;
-        sb = eng->dn_sc + (size_t)expert * H * eng->ss2;
-        qstride = eng->rs2; sstride = eng->ss2; step = 1;
+        qb = eng->dn + (size_t)expert * H * eng->row_bytes();
+        sb = qb + eng->rs2;
+        stride = eng->row_bytes();
     } else {
-        qb = eng->gu_qs + ((size_t)expert * I * 2 + proj) * eng->rs1;
-        sb = eng->gu_sc + ((size_t)expert * I * 2 + proj) * eng->ss1;
-        qstride = eng->rs1; sstride = eng->ss1; step = 2;
+        qb = eng->gu + (size_t)expert * I * eng->unit_bytes() + (size_t)proj * eng->rs1;
+        sb = eng->gu + (size_t)expert * I * eng->unit_bytes() + 2 * (size_t)eng->rs1 + (size_t)proj * eng->ss1;
+        stride = eng->unit_bytes();
     }
     const int64_t warps = rows * (cols / 32);
-    quantize_weight_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
-        src, w_dtype, rows, cols, qb, qstride, step, sb, sstride, step);
+    quantize_weight_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(src, w_dtype, rows, cols, qb,
+                                                                                       sb, stride);
     CUDA_TRY(cudaGetLastError());
     if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
     CUDA_TRY(cudaStreamSynchronize(st));
@@ -576,7 +591,7 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     DeviceGuard g(eng->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (T == 0) return MOE_OK;
-    const int64_t H = eng->cfg.hidden_size;
+    const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
     if (eng->cfg.quant_type == MOE_AWQ) {
         if (int rc = ensure_workspace(eng, T * K)) return rc;
@@ -610,8 +625,11 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         p.y = static_cast<uint8_t*>(y) + (size_t)t0 * H * ye;
         p.ids = topk_ids + t0 * K;
         p.tw = topk_w + t0 * K;
-        p.gu_qs = eng->gu_qs; p.gu_sc = eng->gu_sc; p.dn_qs = eng->dn_qs; p.dn_sc = eng->dn_sc;
-        p.h_ws = eng->h_ws; p.bar = eng->bar; p.err = eng->err;
+        p.gu = eng->gu; p.dn = eng->dn;
+        p.h_ws = eng->h_ws; p.bar = reinterpret_cast<unsigned long long*>(eng->bar); p.err = eng->err;
+        p.hmax = eng->hmax;
+        p.hmax_stride = (int32_t)(eng->h_cap * (I / 32));
+        p.dbg = eng->timeline;
         const int rc = eng->cfg.quant_type == MOE_Q4_0 ? launch_decode<true>(pl, st) : launch_decode<false>(pl, st);
         if (rc) return rc;
     }
@@ -643,7 +661,11 @@ extern "C" int moe_engine_device_error(moe_engine* eng, int32_t* code) {
     int32_t v = 0;
     CUDA_TRY(cudaMemcpy(&v, eng->err, 4, cudaMemcpyDeviceToHost));
     *code = v;
-    if (v != 0) CUDA_TRY(cudaMemset(eng->bar, 0, 256));  // clear error word and barrier state
+    if (v != 0) {  // clear the error word, the barrier state and the block maxima
+        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
+        if (eng->hmax)
+            CUDA_TRY(cudaMemset(eng->hmax, 0, 2 * (size_t)eng->h_cap * (eng->cfg.intermediate_size / 32) * 4));
+    }
     return MOE_OK;
 }
 
@@ -659,14 +681,16 @@ extern "C" int moe_engine_export_expert(moe_engine* eng, int64_t expert, int32_t
     const int64_t rows = which == 0 ? 2 * I : H;
     const int64_t qrow = which == 0 ? (q4 ? H / 2 : H) : (q4 ? I / 2 : I);
     const int64_t srow = which == 0 ? (H / 32) * 2 : (I / 32) * 2;
-    const uint8_t* qsrc = which == 0 ? eng->gu_qs + (size_t)expert * rows * eng->rs1 : eng->dn_qs + (size_t)expert * rows * eng->rs2;
-    const uint8_t* ssrc = which == 0 ? eng->gu_sc + (size_t)expert * rows * eng->ss1 : eng->dn_sc + (size_t)expert * rows * eng->ss2;
+    const int map = which == 0 ? kGateUp : kDown;
+    const uint8_t* base = which == 0 ? eng->gu + (size_t)expert * I * eng->unit_bytes()
+                                     : eng->dn + (size_t)expert * H * eng->row_bytes();
+    const int64_t rec = which == 0 ? eng->unit_bytes() : eng->row_bytes();
     uint8_t *dq = nullptr, *ds = nullptr;
     CUDA_TRY(cudaMalloc(&dq, rows * qrow));
     CUDA_TRY(cudaMalloc(&ds, rows * srow));
-    const int map = which == 0 ? kGateUpInterleave : kIdentity;
-    unpack_rows_kernel<<<(unsigned)rows, 128>>>(dq, qsrc, rows, qrow, which == 0 ? eng->rs1 : eng->rs2, map, I);
-    unpack_rows_kernel<<<(unsigned)rows, 128>>>(ds, ssrc, rows, srow, which == 0 ? eng->ss1 : eng->ss2, map, I);
+    unpack_rows_kernel<<<(unsigned)rows, 128>>>(dq, base, rows, qrow, rec, 0, which == 0 ? eng->rs1 : 0, map, I);
+    unpack_rows_kernel<<<(unsigned)rows, 128>>>(ds, base, rows, srow, rec, which == 0 ? 2 * (int64_t)eng->rs1 : eng->rs2,
+                                                which == 0 ? eng->ss1 : 0, map, I);
     CUDA_TRY(cudaGetLastError());
     CUDA_TRY(cudaMemcpy(qs_out, dq, rows * qrow, cudaMemcpyDeviceToHost));
     CUDA_TRY(cudaMemcpy(d_out, ds, rows * srow, cudaMemcpyDeviceToHost));
@@ -718,5 +742,29 @@ extern "C" int moe_quantize_rows_q8_0(const void* x, int32_t dtype, int64_t rows
     quantize_rows_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         x, dtype, rows, cols, qs, d);
     CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64_t* out, int32_t max_entries,
+                                         int32_t* n_entries) {
+    if (int rc = check_engine(eng)) return rc;
+    DeviceGuard g(eng->cfg.device);
+    if (enable && !eng->timeline) {
+        CUDA_TRY(cudaMalloc(&eng->timeline, (size_t)eng->num_sms * kStamps * sizeof(unsigned long long)));
+        CUDA_TRY(cudaMemset(eng->timeline, 0, (size_t)eng->num_sms * kStamps * sizeof(unsigned long long)));
+        eng->timeline_ctas = eng->num_sms;
+    }
+    if (!enable && eng->timeline) {
+        CUDA_TRY(cudaDeviceSynchronize());
+        cudaFree(eng->timeline);
+        eng->timeline = nullptr;
+        eng->timeline_ctas = 0;
+    }
+    if (n_entries) *n_entries = eng->timeline_ctas * kStamps;
+    if (out && eng->timeline) {
+        CUDA_TRY(cudaDeviceSynchronize());
+        const int n = std::min(max_entries, eng->timeline_ctas * kStamps);
+        CUDA_TRY(cudaMemcpy(out, eng->timeline, (size_t)n * 8, cudaMemcpyDeviceToHost));
+    }
     return MOE_OK;
 }

@@ -1,37 +1,39 @@
 // Persistent fused MoE layer kernel for decode-size token counts (Q8_0 / Q4_0).
 //
-// One CTA per SM (cooperative launch).  Per launch:
-//   phase 0  every CTA routes the T*K pairs itself (stable counting sort of
-//            moe_common.cpp:146-184, in shared memory) and quantises the T
-//            token rows to Q8_0 (gemm_kernels.cpp:25-58) into shared memory;
-//   phase 1  gate_up: the U*I "units" (gate row j + up row j of an active
-//            expert) are split into equal contiguous ranges, one per CTA; each
-//            unit's two rows are dotted with the expert's token rows and
-//            SiLU(gate)*up goes to the fp32 workspace h[pos][j];
+// One CTA per SM (cooperative launch), kWarps warps per CTA, no producer warp:
+// every warp streams its own work items with cp.async.bulk into a private ring
+// of shared-memory slots (one mbarrier per slot) and computes on them.
+//   phase 0  every CTA routes the T*K pairs itself (the stable counting sort of
+//            moe_common.cpp:146-184) and quantises the T token rows to Q8_0
+//            (gemm_kernels.cpp:25-58) in shared memory;
+//   phase 1  gate_up: the U*I units (gate row j + up row j of an active expert)
+//            are split into equal contiguous ranges, one per CTA, dealt to its
+//            warps round-robin; a unit's rows are dotted with the expert's token
+//            rows, SiLU(gate)*up goes to the fp32 workspace h[pos][j] and |h| is
+//            max-reduced per 32-block into hmax (global atomics);
 //   barrier  one grid barrier (bounded spin);
-//   phase 2  down: each CTA owns an equal range of the H output rows for ALL
-//            active experts, requantises h (pack_A_q8_0, gemm_kernels.cpp:394-425),
-//            computes out[pos][n] and finally the k-ordered combine
+//   phase 2  every CTA requantises h with the block maxima (pack_A_q8_0,
+//            gemm_kernels.cpp:394-425), computes the down rows [n0,n1) it owns for
+//            ALL active experts and then the k-ordered combine
 //            y[t][n] = sum_k w[t,k] out[pos(t,k)][n] (q8_gemm.cpp:593-613).
-// A producer warp streams every weight chunk of the CTA (phase 1, then phase 2)
-// with cp.async.bulk into a ring of shared-memory stages guarded by mbarriers,
-// so the down-projection weights are already arriving while the CTAs wait at
-// the grid barrier.  Weights cross HBM exactly once per launch.
+// A warp's ring is issued `slots` items ahead across the phase boundary, so the
+// down-projection weights are in flight while the CTAs wait at the grid
+// barrier.  Weights cross HBM exactly once per launch.
 #pragma once
 #include "common.cuh"
 
 namespace moe {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kDecodeThreads = kConsumerThreads + 32;
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
 constexpr int kTokTile = 4;  // token rows held in registers per pass
+constexpr int kStamps = 16;
 
 struct DecodeParams {
-    const uint8_t* gu_qs;  // [E][I][2][rs1]   gate row j, up row j
-    const uint8_t* gu_sc;  // [E][I][2][ss1]   16-bit scale bits
-    const uint8_t* dn_qs;  // [E][H][rs2]
-    const uint8_t* dn_sc;  // [E][H][ss2]
+    // gate_up unit records [E][I]: gate qs row j (rs1) | up qs row j (rs1) | gate scales (ss1) | up scales (ss1)
+    const uint8_t* gu;
+    // down row records [E][H]: qs row n (rs2) | scales (ss2)
+    const uint8_t* dn;
     int32_t rs1, ss1, rs2, ss2;
     int32_t E, e_off, H, I, T, K;
     int32_t scale_bf16, act_bf16, out_kind;  // out_kind: 0 f16, 1 bf16, 2 f32
@@ -39,18 +41,27 @@ struct DecodeParams {
     void* y;
     const int32_t* ids;
     const float* tw;
-    float* h_ws;     // [T*K][I]
-    uint32_t* bar;   // grid barrier {count, generation}
-    int32_t* err;    // device error word
+    float* h_ws;         // [T*K][I]
+    uint32_t* hmax;      // [2][hmax_stride]  |h| maxima per (pos, 32-block), double buffered
+    int32_t hmax_stride; // entries per buffer (>= T*K*I/32)
+    unsigned long long* bar;  // grid barrier arrival counter (monotonic)
+    int32_t* err;        // device error word
     // shared-memory carve-up (bytes)
-    int32_t off_x, off_out, off_stage, stage_bytes, nstages;
-    int32_t units_per_chunk;   // phase-1 units per stage
-    int32_t rows_max;          // phase-2 rows per CTA (upper bound)
-    int32_t experts_per_chunk; // phase-2 experts per stage
-    int32_t lanes_per_row;     // phase-2 lanes per down row (power of two)
+    int32_t off_x, off_out, off_ring, slot_bytes, slots;
+    int32_t rows_max;       // phase-2 rows per CTA (upper bound)
+    int32_t lanes_per_row;  // phase-2 lanes per down row (power of two)
+    int32_t units_per_item; // phase-1 gate/up units per bulk copy (1, 2 or 4)
+    unsigned long long* dbg;  // optional per-CTA phase stamps [grid][kStamps] (globaltimer ns)
 };
 
-// Shared routing tables, placed at the start of dynamic shared memory.
+MOE_DEV unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+MOE_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 struct RouteSmem {
     int32_t* ids;    // [TK] local expert id or -1
     int32_t* smap;   // [TK] position or -1
@@ -102,29 +113,37 @@ MOE_DEV void route_warp(const int32_t* g_ids, int TK, int E, int e_off, RouteSme
         if (e >= 0 && rank == 0) r.cnt[e] = base + __popc(peers);
         __syncwarp();
     }
-    // exclusive scan of counts -> start, and the unique-expert list
-    int carry = 0, ucarry = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) {
-        const int e = e0 + lane;
-        const int c = (e < E) ? r.cnt[e] : 0;
-        int incl = c;
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-        }
-        const unsigned act = __ballot_sync(0xffffffffu, c > 0);
-        if (e < E) {
-            r.start[e] = carry + incl - c;
-            if (c > 0) {
-                const int u = ucarry + __popc(act & ((1u << lane) - 1u));
-                r.ue[u] = e;
-                r.ups[u] = carry + incl - c;
-                r.ucnt[u] = c;
-            }
-        }
-        carry += __shfl_sync(0xffffffffu, incl, 31);
-        ucarry += __popc(act);
+    // exclusive scan of counts -> start, and the unique-expert list: lane l owns the
+    // contiguous experts [l*c, l*c + c); one warp scan of (actives << 16 | count).
+    const int c = (E + 31) >> 5;
+    int loc = 0;
+    for (int k = 0; k < c; ++k) {
+        const int e = lane * c + k;
+        const int n = e < E ? r.cnt[e] : 0;
+        loc += (n > 0 ? (1 << 16) : 0) + n;
     }
+    int incl = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    int run = incl - loc;  // exclusive prefix of this lane's chunk
+    for (int k = 0; k < c; ++k) {
+        const int e = lane * c + k;
+        if (e >= E) break;
+        const int n = r.cnt[e];
+        const int pos0 = run & 0xffff, u = run >> 16;
+        r.start[e] = pos0;
+        if (n > 0) {
+            r.ue[u] = e;
+            r.ups[u] = pos0;
+            r.ucnt[u] = n;
+        }
+        run += (n > 0 ? (1 << 16) : 0) + n;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    const int carry = total & 0xffff, ucarry = total >> 16;
     if (lane == 0) {
         r.start[E] = carry;
         *r.nuniq = ucarry;
@@ -144,48 +163,94 @@ MOE_DEV void route_warp(const int32_t* g_ids, int TK, int E, int e_off, RouteSme
 // Q4_0 activation byte order inside a 32-block: the weight word w holds
 // elements 8w..8w+7 in nibbles 0..7, so its low nibbles are elements
 // 8w+{0,2,4,6} and its high nibbles 8w+{1,3,5,7}.
+// Q4_0 activation byte order inside a 32-block: the weight word w holds
+// elements 8w..8w+7 in nibbles 0..7, so its low nibbles are elements
+// 8w+{0,2,4,6} and its high nibbles 8w+{1,3,5,7}.
 MOE_DEV int q4_perm(int e) {
     const int w = e >> 3, r = e & 7;
     return (w << 3) + ((r & 1) << 2) + (r >> 1);
 }
 
-// Quantise `nrows` rows of `cols` values (fp32 in global via a loader) into
-// shared memory, 8 lanes per 32-block, each lane 4 consecutive values.
-template <bool Q4, typename Loader>
-MOE_DEV void quant_rows_smem(Loader load4, int nrows, int cols, int8_t* q, float* d, int32_t* s,
-                             int tid, int nthreads) {
-    const int nb = cols >> 5;
-    const int ngroups = nrows * nb;
-    // every block needs all 8 lanes of its group: iterate in whole groups
-    for (int base = (tid >> 3); base < ((ngroups + (nthreads >> 3) - 1) / (nthreads >> 3)) * (nthreads >> 3);
-         base += (nthreads >> 3)) {
-        const int sub = tid & 7;
-        const bool valid = base < ngroups;
-        const int row = valid ? base / nb : 0, b = valid ? base % nb : 0;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (valid) load4(row, b * 32 + sub * 4, v);
-        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        const float dd = q8_scale(amax);
-        const float id = q8_inv(dd);
-        int qsum = 0;
-        int8_t* qb = q + (size_t)row * cols + b * 32;
+// Quantise one 32-block held by one thread (v[32]) with scale d into 8 packed
+// 32-bit words (Q4: the permuted activation order, Q8: natural order) and
+// return the sum of the quantised values.
+template <bool Q4>
+MOE_DEV int quant_block_store(const float* v, float d, int8_t* qb) {
+    const float id = q8_inv(d);
+    int q[32];
+    int sum = 0;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int qq = q8_quant(v[j], id);
-            qsum += qq;
-            const int e = sub * 4 + j;
-            if (valid) qb[Q4 ? q4_perm(e) : e] = (int8_t)qq;
+    for (int e = 0; e < 32; ++e) {
+        q[e] = q8_quant(v[e], id);
+        sum += q[e];
+    }
+    uint32_t wv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int e = Q4 ? 8 * (k >> 1) + (k & 1) + 2 * i : 4 * k + i;
+            w |= (uint32_t)(q[e] & 0xff) << (8 * i);
         }
-        qsum += __shfl_xor_sync(0xffffffffu, qsum, 4);
-        qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
-        qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-        if (valid && sub == 0) {
-            d[row * nb + b] = dd;
-            if (Q4) s[row * nb + b] = qsum;
+        wv[k] = w;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(qb);
+    dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+    return sum;
+}
+
+// Token rows -> Q8_0 in shared memory, one thread per 32-block (no shuffles,
+// one global round trip per block).
+template <bool Q4>
+MOE_DEV void quant_x_smem(const uint8_t* x, int act_bf16, int nrows, int cols, int8_t* q, float* d, int32_t* s,
+                          int tid, int nthreads) {
+    const int nb = cols >> 5;
+    const int nblk = nrows * nb;
+    for (int g = tid; g < nblk; g += nthreads) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)g * 64);  // rows contiguous: block g at g*32
+        uint4 raw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) raw[k] = __ldg(src + k);
+        float v[32];
+        float amax = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t w4[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[8 * k + 2 * i] = scale_to_f32((uint16_t)(w4[i] & 0xffffu), act_bf16);
+                v[8 * k + 2 * i + 1] = scale_to_f32((uint16_t)(w4[i] >> 16), act_bf16);
+            }
         }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        const float dd = q8_scale(amax);
+        const int sum = quant_block_store<Q4>(v, dd, q + (size_t)g * 32);
+        d[g] = dd;
+        if (Q4) s[g] = sum;
+    }
+}
+
+// Requantise h [P][I] (fp32, global) with the per-block maxima `hmax`, one
+// thread per 32-block: the scale needs no reduction (pack_A_q8_0 rule).
+template <bool Q4>
+MOE_DEV void requant_h_smem(const float* h, const uint32_t* hmax, int P, int I, int8_t* q, float* d, int32_t* s,
+                            int tid) {
+    const int nblk = P * (I >> 5);
+    for (int g = tid; g < nblk; g += kThreads) {
+        const float4* src = reinterpret_cast<const float4*>(h + (size_t)g * 32);
+        float v[32];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 f = __ldcg(src + k);
+            v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+        }
+        const float dd = q8_scale(__uint_as_float(__ldcg(hmax + g)));
+        const int sum = quant_block_store<Q4>(v, dd, q + (size_t)g * 32);
+        d[g] = dd;
+        if (Q4) s[g] = sum;
     }
 }
 
@@ -222,190 +287,221 @@ MOE_DEV int block_dot(const uint4* w, const uint4* a, int asum) {
     }
 }
 
-// Chunk enumeration shared by producer and consumers ------------------------
-struct P1Chunk { int u, j0, n; };
-
-struct P1Iter {
+// Work of one warp.  Phase 1: the warp's contiguous share [u_cur, u_end) of the
+// CTA's units, cut into items of up to `upi` consecutive units of one expert.
+// Phase 2: items (expert ui, group g of RPG rows), it = warp + k*kWarps.
+struct P1Cursor {
     int64_t cur, end;
-    int I, per;
-    MOE_DEV bool next(P1Chunk& c) {
+    int I, upi;
+    // next item: unique expert index u, first unit j0, unit count n
+    MOE_DEV bool next(int& u, int& j0, int& n) {
         if (cur >= end) return false;
-        c.u = (int)(cur / I);
-        c.j0 = (int)(cur % I);
-        int64_t n = end - cur;
-        if (n > I - c.j0) n = I - c.j0;
-        if (n > per) n = per;
-        c.n = (int)n;
-        cur += n;
+        u = (int)(cur / I);
+        j0 = (int)(cur - (int64_t)u * I);
+        int64_t m = end - cur;
+        if (m > I - j0) m = I - j0;
+        if (m > upi) m = upi;
+        n = (int)m;
+        cur += m;
         return true;
     }
 };
 
+struct P2Work {
+    int n2, ngrp, RPG, R, n0;
+};
+
+MOE_DEV void issue_p1(const DecodeParams& p, const RouteSmem& rt, int u, int j0, int n, uint8_t* slot, uint64_t* bar) {
+    const uint32_t ub = 2u * (p.rs1 + p.ss1);
+    mbar_arrive_expect_tx(bar, ub * n);
+    bulk_g2s(slot, p.gu + ((size_t)rt.ue[u] * p.I + j0) * ub, ub * n, bar);
+}
+
+MOE_DEV void issue_p2(const DecodeParams& p, const RouteSmem& rt, const P2Work& w2, int it, uint8_t* slot,
+                      uint64_t* bar) {
+    const int ui = it / w2.ngrp, g = it - ui * w2.ngrp;
+    const int r0 = g * w2.RPG;
+    const int rows = min(w2.RPG, w2.R - r0);
+    const uint32_t rb = (uint32_t)(p.rs2 + p.ss2);
+    mbar_arrive_expect_tx(bar, rows * rb);
+    bulk_g2s(slot, p.dn + ((size_t)rt.ue[ui] * p.H + w2.n0 + r0) * rb, rows * rb, bar);
+}
+
 template <bool Q4>
-__global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const int TK = p.T * p.K, E = p.E, H = p.H, I = p.I;
     const int nb1 = H >> 5, nb2 = I >> 5;
+    unsigned long long* dbg = p.dbg ? p.dbg + (size_t)cta * kStamps : nullptr;
+    if (dbg && tid == 0) { dbg[0] = global_ns(); dbg[13] = clock64(); }
 
     RouteSmem rt = carve_route(reinterpret_cast<int32_t*>(smem), TK, E);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_stage - 16 * p.nstages);
-    uint64_t* empty = full + p.nstages;
-    uint8_t* stages = smem + p.off_stage;
-    __shared__ int s_ok;
-
-    // ---------------- phase 0: routing + barrier init (all warps) --------------
-    if (warp == 0) route_warp(p.ids, TK, E, p.e_off, rt, lane);
-    if (tid == 32) {
-        for (int s = 0; s < p.nstages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        fence_barrier_init();
-        s_ok = 1;
-    }
-    __syncthreads();
-    const int U = *rt.nuniq;
-
-    // phase-1 range of units and phase-2 range of rows owned by this CTA
-    const int64_t TU = (int64_t)U * I;
-    const int64_t u_begin = TU * cta / G, u_end = TU * (cta + 1) / G;
-    const int n0 = (int)((int64_t)H * cta / G), n1 = (int)((int64_t)H * (cta + 1) / G);
-    const int R = n1 - n0;
-    const int nchunk2 = (R > 0 && U > 0) ? (U + p.experts_per_chunk - 1) / p.experts_per_chunk : 0;
-
-    if (warp == kConsumerWarps) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            int s = 0;
-            uint32_t ph = 0;
-            P1Iter it{u_begin, u_end, I, p.units_per_chunk};
-            P1Chunk c;
-            bool ok = true;
-            while (ok && it.next(c)) {
-                if (!mbar_wait(&empty[s], ph ^ 1)) { atomicExch(p.err, kErrEmptyWait); ok = false; break; }
-                const int e = rt.ue[c.u];
-                const uint32_t qb = (uint32_t)c.n * 2u * p.rs1, sb = (uint32_t)c.n * 2u * p.ss1;
-                uint8_t* dst = stages + (size_t)s * p.stage_bytes;
-                mbar_arrive_expect_tx(&full[s], qb + sb);
-                bulk_g2s(dst, p.gu_qs + ((size_t)e * I + c.j0) * 2 * p.rs1, qb, &full[s]);
-                bulk_g2s(dst + qb, p.gu_sc + ((size_t)e * I + c.j0) * 2 * p.ss1, sb, &full[s]);
-                if (++s == p.nstages) { s = 0; ph ^= 1; }
-            }
-            for (int ch = 0; ok && ch < nchunk2; ++ch) {
-                if (!mbar_wait(&empty[s], ph ^ 1)) { atomicExch(p.err, kErrEmptyWait); ok = false; break; }
-                const int ua = ch * p.experts_per_chunk;
-                const int ub = min(U, ua + p.experts_per_chunk);
-                const uint32_t qrow = (uint32_t)R * p.rs2, srow = (uint32_t)R * p.ss2;
-                uint8_t* dst = stages + (size_t)s * p.stage_bytes;
-                const uint32_t qtot = (uint32_t)(ub - ua) * qrow;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)(ub - ua) * (qrow + srow));
-                for (int u = ua; u < ub; ++u) {
-                    const int e = rt.ue[u];
-                    bulk_g2s(dst + (size_t)(u - ua) * qrow, p.dn_qs + ((size_t)e * H + n0) * p.rs2, qrow, &full[s]);
-                    bulk_g2s(dst + qtot + (size_t)(u - ua) * srow, p.dn_sc + ((size_t)e * H + n0) * p.ss2, srow,
-                             &full[s]);
-                }
-                if (++s == p.nstages) { s = 0; ph ^= 1; }
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumers ----------------
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_ring - 8 * kWarps * p.slots);
+    uint64_t* mybar = bars + warp * p.slots;
+    uint8_t* myring = smem + p.off_ring + (size_t)warp * p.slots * p.slot_bytes;
     int8_t* xq = reinterpret_cast<int8_t*>(smem + p.off_x);
     float* xd = reinterpret_cast<float*>(xq + (size_t)p.T * H);
     int32_t* xs = reinterpret_cast<int32_t*>(xd + (size_t)p.T * nb1);
-    {
-        const void* x = p.x;
-        const int bf = p.act_bf16;
-        auto load4 = [&](int row, int col, float* v) {
-            const int64_t base = (int64_t)row * H + col;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = act_to_f32(x, base + j, bf);
-        };
-        quant_rows_smem<Q4>(load4, p.T, H, xq, xd, xs, tid, kConsumerThreads);
+    __shared__ int s_ok;
+    __shared__ unsigned long long s_launch;
+
+    // ---------------- phase 0 ----------------
+    if (lane == 0)
+        for (int s = 0; s < p.slots; ++s) mbar_init(&mybar[s], 1);
+    if (warp == kWarps - 1) {  // one warp routes while the others quantise the tokens
+        route_warp(p.ids, TK, E, p.e_off, rt, lane);
+        if (lane == 0) {
+            s_ok = 1;
+            s_launch = barrier_launch_index(p.bar, (uint32_t)G);  // selects this launch's hmax buffer
+            if (dbg) dbg[1] = global_ns();
+        }
+    } else {
+        quant_x_smem<Q4>(static_cast<const uint8_t*>(p.x), p.act_bf16, p.T, H, xq, xd, xs, tid, kThreads - 32);
+        if (dbg && tid == 0) dbg[2] = global_ns();
     }
-    named_bar_sync(1, kConsumerThreads);
+    fence_barrier_init();
+    __syncthreads();
+    if (dbg && tid == 0) dbg[3] = global_ns();
+
+    const int U = *rt.nuniq;
+    const unsigned long long launch = s_launch;
+    const uint32_t par = (uint32_t)(launch & 1ull);
+    uint32_t* hmax = p.hmax + (size_t)par * p.hmax_stride;
+
+    // this warp's phase-1 share and phase-2 items
+    const int64_t TU = (int64_t)U * I;
+    const int64_t cb = TU * cta / G, ce = TU * (cta + 1) / G;
+    P1Cursor c_issue{cb + (ce - cb) * warp / kWarps, cb + (ce - cb) * (warp + 1) / kWarps, I, p.units_per_item};
+    P1Cursor c_use = c_issue;
+    P2Work w2;
+    w2.n0 = (int)((int64_t)H * cta / G);
+    w2.R = (int)((int64_t)H * (cta + 1) / G) - w2.n0;
+    w2.RPG = 32 / p.lanes_per_row;
+    w2.ngrp = (w2.R + w2.RPG - 1) / w2.RPG;
+    const int tot2 = U * w2.ngrp;
+    w2.n2 = warp < tot2 ? (tot2 - warp + kWarps - 1) / kWarps : 0;
+    int issued2 = 0;  // phase-2 items issued so far
+
+    // issue the first `slots` items (phase 1, then phase 2) of this warp
+    int n_inflight = 0;
+    if (lane == 0) {
+        int u, j0, n;
+        while (n_inflight < p.slots && c_issue.next(u, j0, n)) {
+            issue_p1(p, rt, u, j0, n, myring + (size_t)n_inflight * p.slot_bytes, &mybar[n_inflight]);
+            ++n_inflight;
+        }
+        while (n_inflight < p.slots && issued2 < w2.n2) {
+            issue_p2(p, rt, w2, warp + issued2 * kWarps, myring + (size_t)n_inflight * p.slot_bytes, &mybar[n_inflight]);
+            ++issued2;
+            ++n_inflight;
+        }
+    }
+    // lane 0 advances its cursors; keep the other lanes' copies in step
+    c_issue.cur = __shfl_sync(0xffffffffu, c_issue.cur, 0);
+    issued2 = __shfl_sync(0xffffffffu, issued2, 0);
+
+    auto refill = [&](int s) {  // after consuming slot s: issue this warp's next item into it
+        __syncwarp();  // every lane's reads of slot s are complete before lane 0 reuses it
+        if (lane == 0) {
+            int u, j0, n;
+            if (c_issue.next(u, j0, n)) {
+                issue_p1(p, rt, u, j0, n, myring + (size_t)s * p.slot_bytes, &mybar[s]);
+            } else if (issued2 < w2.n2) {
+                issue_p2(p, rt, w2, warp + issued2 * kWarps, myring + (size_t)s * p.slot_bytes, &mybar[s]);
+                if (dbg && warp == 0 && issued2 == 0) dbg[15] = global_ns();
+                ++issued2;
+            }
+        }
+        c_issue.cur = __shfl_sync(0xffffffffu, c_issue.cur, 0);
+        issued2 = __shfl_sync(0xffffffffu, issued2, 0);
+    };
 
     const bool sbf = p.scale_bf16 != 0;
-    int s = 0;
-    uint32_t ph = 0;
     bool ok = true;
+    int item = 0;
 
     // ---------------- phase 1: gate_up + SiLU*up ----------------
     {
-        P1Iter it{u_begin, u_end, I, p.units_per_chunk};
-        P1Chunk c;
-        while (it.next(c)) {
-            if (!mbar_wait(&full[s], ph)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
-            const uint8_t* st = stages + (size_t)s * p.stage_bytes;
-            const uint8_t* qbase = st;
-            const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + (size_t)c.n * 2 * p.rs1);
-            const int ps = rt.ups[c.u], cnt = rt.ucnt[c.u];
-            for (int jj = warp; jj < c.n; jj += kConsumerWarps) {
-                const uint8_t* qg = qbase + (size_t)jj * 2 * p.rs1;
-                const uint8_t* qu = qg + p.rs1;
-                const uint16_t* sgate = reinterpret_cast<const uint16_t*>(
-                    reinterpret_cast<const uint8_t*>(sbase) + (size_t)jj * 2 * p.ss1);
-                const uint16_t* sup = reinterpret_cast<const uint16_t*>(
-                    reinterpret_cast<const uint8_t*>(sgate) + p.ss1);
-                for (int m0 = 0; m0 < cnt; m0 += kTokTile) {
-                    float ag[kTokTile], au[kTokTile];
-                    int tk[kTokTile];
+        const int LPU = 32 / p.units_per_item;  // lanes per unit
+        const int usub = lane % LPU, uslot = lane / LPU;
+        int u, j0, n;
+        while (c_use.next(u, j0, n)) {
+            const int s = item % p.slots;
+            if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
+            if (dbg && tid == 0) dbg[item == 0 ? 4 : 5] = global_ns();
+            const bool valid = uslot < n;
+            const uint8_t* rec = myring + (size_t)s * p.slot_bytes + (size_t)(valid ? uslot : 0) * 2 * (p.rs1 + p.ss1);
+            const uint8_t* qg = rec;
+            const uint8_t* qu = rec + p.rs1;
+            const uint16_t* sgate = reinterpret_cast<const uint16_t*>(rec + 2 * p.rs1);
+            const uint16_t* sup = reinterpret_cast<const uint16_t*>(rec + 2 * p.rs1 + p.ss1);
+            const int j = j0 + uslot;
+            const int ps = rt.ups[u], cnt = rt.ucnt[u];
+            for (int m0 = 0; m0 < cnt; m0 += kTokTile) {  // up to kTokTile tokens per weight load
+                const int nt = min(kTokTile, cnt - m0);
+                int tk[kTokTile];
+                float ag[kTokTile], au[kTokTile];
 #pragma unroll
-                    for (int m = 0; m < kTokTile; ++m) {
-                        ag[m] = 0.f;
-                        au[m] = 0.f;
-                        tk[m] = (m0 + m < cnt) ? rt.tok[ps + m0 + m] / p.K : -1;
-                    }
-                    for (int b = lane; b < nb1; b += 32) {
+                for (int m = 0; m < kTokTile; ++m) {
+                    tk[m] = m < nt ? rt.tok[ps + m0 + m] / p.K : 0;
+                    ag[m] = 0.f;
+                    au[m] = 0.f;
+                }
+                if (valid) {
+#pragma unroll 2
+                    for (int b = usub; b < nb1; b += LPU) {
                         const uint4* wg = reinterpret_cast<const uint4*>(qg + (size_t)b * (Q4 ? 16 : 32));
                         const uint4* wu = reinterpret_cast<const uint4*>(qu + (size_t)b * (Q4 ? 16 : 32));
                         const float dg = scale_to_f32(sgate[b], sbf), du = scale_to_f32(sup[b], sbf);
 #pragma unroll
                         for (int m = 0; m < kTokTile; ++m) {
-                            if (tk[m] < 0) continue;
-                            const uint4* a = reinterpret_cast<const uint4*>(xq + (size_t)tk[m] * H + b * 32);
-                            const float ad = xd[tk[m] * nb1 + b];
-                            const int as = Q4 ? xs[tk[m] * nb1 + b] : 0;
-                            const int ig = block_dot<Q4>(wg, a, as);
-                            const int iu = block_dot<Q4>(wu, a, as);
-                            ag[m] += ((float)ig * dg) * ad;
-                            au[m] += ((float)iu * du) * ad;
+                            if (m >= nt) break;
+                            const int t = tk[m];
+                            const uint4* a = reinterpret_cast<const uint4*>(xq + (size_t)t * H + b * 32);
+                            const float ad = xd[t * nb1 + b];
+                            const int as = Q4 ? xs[t * nb1 + b] : 0;
+                            ag[m] += ((float)block_dot<Q4>(wg, a, as) * dg) * ad;
+                            au[m] += ((float)block_dot<Q4>(wu, a, as) * du) * ad;
                         }
-                    }
-#pragma unroll
-                    for (int m = 0; m < kTokTile; ++m) {
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) {
-                            ag[m] += __shfl_xor_sync(0xffffffffu, ag[m], o);
-                            au[m] += __shfl_xor_sync(0xffffffffu, au[m], o);
-                        }
-                    }
-                    if (lane < kTokTile && m0 + lane < cnt) {
-                        float g = ag[0], u = au[0];
-#pragma unroll
-                        for (int m = 1; m < kTokTile; ++m)
-                            if (lane == m) { g = ag[m]; u = au[m]; }
-                        p.h_ws[(size_t)(ps + m0 + lane) * I + c.j0 + jj] = silu_mul(g, u);
                     }
                 }
+#pragma unroll
+                for (int m = 0; m < kTokTile; ++m) {
+                    if (m >= nt) break;  // uniform within the warp
+                    for (int o = LPU >> 1; o > 0; o >>= 1) {
+                        ag[m] += __shfl_xor_sync(0xffffffffu, ag[m], o);
+                        au[m] += __shfl_xor_sync(0xffffffffu, au[m], o);
+                    }
+                }
+                // lane usub == m of each unit group finishes token m
+                if (valid && usub < nt) {
+                    float g = ag[0], uu = au[0];
+#pragma unroll
+                    for (int m = 1; m < kTokTile; ++m)
+                        if (usub == m) { g = ag[m]; uu = au[m]; }
+                    const float hv = silu_mul(g, uu);
+                    const int pos = ps + m0 + usub;
+                    p.h_ws[(size_t)pos * I + j] = hv;
+                    atomicMax(hmax + (size_t)pos * nb2 + (j >> 5), __float_as_uint(fabsf(hv)));
+                }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == p.nstages) { s = 0; ph ^= 1; }
+            refill(s);
+            ++item;
         }
     }
+    if (dbg && tid == 0) dbg[6] = global_ns();
 
     // ---------------- grid barrier ----------------
-    named_bar_sync(1, kConsumerThreads);
-    if (tid == 0) {
-        if (!ok || !grid_barrier(p.bar, (uint32_t)G, p.err)) s_ok = 0;
+    __syncthreads();
+    if (dbg && tid == 0) dbg[7] = global_ns();
+    if (tid == 1) {  // a lane that issues no bulk copies: its release waits on no copy in flight
+        if (!grid_barrier(p.bar, (uint32_t)G, (launch + 1ull) * (uint32_t)G, p.err)) s_ok = 0;
     }
-    named_bar_sync(1, kConsumerThreads);
+    __syncthreads();
     ok = ok && s_ok;
+    if (dbg && tid == 0) dbg[8] = global_ns();
 
     // ---------------- phase 2: requant h, down rows, combine ----------------
     const int P = rt.start[E];
@@ -413,73 +509,72 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const Dec
     float* hd = reinterpret_cast<float*>(hq + (size_t)P * I);
     int32_t* hs = reinterpret_cast<int32_t*>(hd + (size_t)P * nb2);
     float* outs = reinterpret_cast<float*>(smem + p.off_out);
-    if (ok && nchunk2 > 0) {
-        const float* h = p.h_ws;
-        auto load4 = [&](int row, int col, float* v) {
-            const float4 f = __ldcg(reinterpret_cast<const float4*>(h + (size_t)row * I + col));
-            v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-        };
-        quant_rows_smem<Q4>(load4, P, I, hq, hd, hs, tid, kConsumerThreads);
+    if (ok && w2.R > 0 && U > 0) requant_h_smem<Q4>(p.h_ws, hmax, P, I, hq, hd, hs, tid);
+    {   // clear the other hmax buffer for the next launch (no CTA reads it in this launch)
+        uint32_t* other = p.hmax + (size_t)(par ^ 1u) * p.hmax_stride;
+        for (int i = cta * kThreads + tid; i < p.hmax_stride; i += G * kThreads) other[i] = 0u;
     }
-    named_bar_sync(1, kConsumerThreads);
+    __syncthreads();
+    if (dbg && tid == 0) dbg[9] = global_ns();
 
-    const int LPR = p.lanes_per_row, RPG = 32 / LPR;
+    const int LPR = p.lanes_per_row;
     const int sub = lane % LPR, rr = lane / LPR;
-    const int ngrp = (R + RPG - 1) / RPG;
-    for (int ch = 0; ch < nchunk2; ++ch) {
-        if (!ok) break;
-        if (!mbar_wait(&full[s], ph)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
-        const uint8_t* st = stages + (size_t)s * p.stage_bytes;
-        const int ua = ch * p.experts_per_chunk;
-        const int ub = min(U, ua + p.experts_per_chunk);
-        const size_t qrow = (size_t)R * p.rs2, srow = (size_t)R * p.ss2;
-        const size_t qtot = (size_t)(ub - ua) * qrow;
-        const int nitems = (ub - ua) * ngrp;
-        for (int item = warp; item < nitems; item += kConsumerWarps) {
-            const int ui = item / ngrp, g = item % ngrp;
-            const int u = ua + ui;
-            const int row = g * RPG + rr;
-            const bool rv = row < R;
-            const uint8_t* wrow = st + ui * qrow + (size_t)(rv ? row : 0) * p.rs2;
-            const uint16_t* srw = reinterpret_cast<const uint16_t*>(st + qtot + ui * srow + (size_t)(rv ? row : 0) * p.ss2);
-            const int ps = rt.ups[u], cnt = rt.ucnt[u];
-            for (int m0 = 0; m0 < cnt; m0 += kTokTile) {
-                float acc[kTokTile];
+    for (int k2 = 0; ok && k2 < w2.n2; ++k2) {
+        const int s = item % p.slots;
+        if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
+        if (dbg && tid == 0 && k2 == 0) dbg[10] = global_ns();
+        const uint8_t* st = myring + (size_t)s * p.slot_bytes;
+        const int it = warp + k2 * kWarps;
+        const int ui = it / w2.ngrp, g = it - ui * w2.ngrp;
+        const int row = g * w2.RPG + rr;
+        const bool rv = row < w2.R;
+        const uint8_t* wrow = st + (size_t)rr * (p.rs2 + p.ss2);
+        const uint16_t* srw = reinterpret_cast<const uint16_t*>(wrow + p.rs2);
+        const int ps = rt.ups[ui], cnt = rt.ucnt[ui];
+        for (int m0 = 0; m0 < cnt; m0 += kTokTile) {
+            const int nt = min(kTokTile, cnt - m0);
+            float acc[kTokTile];
 #pragma unroll
-                for (int m = 0; m < kTokTile; ++m) acc[m] = 0.f;
-                if (rv) {
-                    for (int b = sub; b < nb2; b += LPR) {
-                        const uint4* w = reinterpret_cast<const uint4*>(wrow + (size_t)b * (Q4 ? 16 : 32));
-                        const float dw = scale_to_f32(srw[b], sbf);
+            for (int m = 0; m < kTokTile; ++m) acc[m] = 0.f;
+            if (rv) {
+#pragma unroll 2
+                for (int b = sub; b < nb2; b += LPR) {
+                    const uint4* w = reinterpret_cast<const uint4*>(wrow + (size_t)b * (Q4 ? 16 : 32));
+                    const float dw = scale_to_f32(srw[b], sbf);
 #pragma unroll
-                        for (int m = 0; m < kTokTile; ++m) {
-                            if (m0 + m >= cnt) continue;
-                            const int pos = ps + m0 + m;
-                            const uint4* a = reinterpret_cast<const uint4*>(hq + (size_t)pos * I + b * 32);
-                            const int is = block_dot<Q4>(w, a, Q4 ? hs[pos * nb2 + b] : 0);
-                            acc[m] += ((float)is * dw) * hd[pos * nb2 + b];
-                        }
+                    for (int m = 0; m < kTokTile; ++m) {
+                        if (m >= nt) break;
+                        const int pos = ps + m0 + m;
+                        const uint4* a = reinterpret_cast<const uint4*>(hq + (size_t)pos * I + b * 32);
+                        const int is = block_dot<Q4>(w, a, Q4 ? hs[pos * nb2 + b] : 0);
+                        acc[m] += ((float)is * dw) * hd[pos * nb2 + b];
                     }
                 }
+            }
+#pragma unroll
+            for (int m = 0; m < kTokTile; ++m) {
+                if (m >= nt) break;
+                for (int o = LPR >> 1; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+            }
+            if (rv && sub == 0) {
 #pragma unroll
                 for (int m = 0; m < kTokTile; ++m)
-                    for (int o = LPR >> 1; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-                if (rv && sub == 0) {
-#pragma unroll
-                    for (int m = 0; m < kTokTile; ++m)
-                        if (m0 + m < cnt) outs[(size_t)(ps + m0 + m) * p.rows_max + row] = acc[m];
-                }
+                    if (m < nt) outs[(size_t)(ps + m0 + m) * p.rows_max + row] = acc[m];
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++s == p.nstages) { s = 0; ph ^= 1; }
+        refill(s);
+        ++item;
     }
-    named_bar_sync(1, kConsumerThreads);
+    // drain: a warp that stopped early still waits (bounded) for its copies in flight
+    if (!ok && lane == 0)
+        for (int i = item; i < item + p.slots; ++i) mbar_wait(&mybar[i % p.slots], (uint32_t)(i / p.slots) & 1u);
+    __syncthreads();
+    if (dbg && tid == 0) dbg[11] = global_ns();
     if (!ok) return;
 
     // combine in k order (q8_gemm.cpp:593-613) and cast (q8_gemm.cpp:636-639)
-    for (int idx = tid; idx < p.T * R; idx += kConsumerThreads) {
+    const int R = w2.R, n0 = w2.n0;
+    for (int idx = tid; idx < p.T * R; idx += kThreads) {
         const int t = idx / R, r = idx % R;
         float acc = 0.f;
         for (int k = 0; k < p.K; ++k) {
@@ -492,6 +587,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) moe_decode_kernel(const Dec
         else if (p.out_kind == 1) reinterpret_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(acc);
         else reinterpret_cast<__half*>(p.y)[o] = __float2half_rn(acc);
     }
+    if (dbg && tid == 0) { dbg[12] = global_ns(); dbg[14] = clock64(); }
 }
 
 }  // namespace moe
