@@ -103,9 +103,11 @@ int moe_engine_last_time_ms(moe_engine* eng, double* ms);
  * *code = 0 when every kernel completed; non-zero when a bounded wait expired. */
 int moe_engine_device_error(moe_engine* eng, int32_t* code);
 
-/* Decode the engine's device-resident weights of one expert back into the row-major
- * input contract (bit-exact check of the load-time packing).  which: 0 gate_up, 1 down.
- * qs_out / d_out are host buffers of the input-contract sizes. */
+/* Decode the engine's device-resident weights of one expert back into row-major form
+ * (bit-exact check of the load-time packing).  which: 0 gate_up (2I rows of H), 1 down
+ * (H rows of I).  Q8_0/Q4_0: qs_out / d_out receive the input-contract rows.  AWQ: qs_out
+ * receives per row the K/2 bytes of sequential nibbles (element k at byte k/2, low nibble
+ * for even k), d_out per row the K/G bf16 scales followed by the K/G zero points (u8). */
 int moe_engine_export_expert(moe_engine* eng, int64_t expert, int32_t which, void* qs_out,
                              void* d_out);
 

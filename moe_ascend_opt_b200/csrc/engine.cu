@@ -10,7 +10,6 @@
 #include <vector>
 
 #include "../../include/moe_b200.h"
-#include "awq.cuh"
 #include "common.cuh"
 #include "moe_decode.cuh"
 
@@ -48,10 +47,9 @@ struct moe_engine {
     // down row records [E][H]: qs row | scales
     uint8_t* dn = nullptr;
     int rs1 = 0, ss1 = 0, rs2 = 0, ss2 = 0;
+    // AWQ: per-row scale field = [bf16 scales x ngroups][u8 zeros x ngroups], padded
     int64_t unit_bytes() const { return 2 * (int64_t)(rs1 + ss1); }
     int64_t row_bytes() const { return (int64_t)(rs2 + ss2); }
-    // AWQ device layout
-    AwqWeights awq{};
     // workspace
     float* h_ws = nullptr;
     int64_t h_cap = 0;  // positions
@@ -297,11 +295,21 @@ int stage_to_device(const void* src, size_t bytes, int on_device, cudaStream_t s
 
 int alloc_q_layout(moe_engine* eng) {
     const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
-    const bool q4 = eng->cfg.quant_type == MOE_Q4_0;
-    eng->rs1 = (int)round_up(q4 ? H / 2 : H, 16);
-    eng->ss1 = (int)round_up((H / 32) * 2, 16);
-    eng->rs2 = (int)round_up(q4 ? I / 2 : I, 16);
-    eng->ss2 = (int)round_up((I / 32) * 2, 16);
+    const int qt = eng->cfg.quant_type;
+    if (qt == MOE_AWQ) {
+        const int64_t G = eng->cfg.group_size;
+        eng->rs1 = (int)round_up(H / 2, 16);
+        eng->ss1 = (int)round_up((H / G) * 3, 16);
+        eng->rs2 = (int)round_up(I / 2, 16);
+        eng->ss2 = (int)round_up((I / G) * 3, 16);
+        eng->scale_bf16 = 1;
+    } else {
+        const bool q4 = qt == MOE_Q4_0;
+        eng->rs1 = (int)round_up(q4 ? H / 2 : H, 16);
+        eng->ss1 = (int)round_up((H / 32) * 2, 16);
+        eng->rs2 = (int)round_up(q4 ? I / 2 : I, 16);
+        eng->ss2 = (int)round_up((I / 32) * 2, 16);
+    }
     if (!eng->gu) {
         CUDA_TRY(cudaMalloc(&eng->gu, (size_t)E * I * eng->unit_bytes()));
         CUDA_TRY(cudaMalloc(&eng->dn, (size_t)E * H * eng->row_bytes()));
@@ -309,6 +317,53 @@ int alloc_q_layout(moe_engine* eng) {
         CUDA_TRY(cudaMemset(eng->dn, 0, (size_t)E * H * eng->row_bytes()));
     }
     return MOE_OK;
+}
+
+// AWQ GEMM packing -> records.  qw [E][Kd][N/8] int32, output column n, input row k:
+// word n/8, nibble position kAwqPos[n%8].  gate_up (N = 2I): column n < I is gate row
+// n of unit n, column I + j is up row j; down (N = H): column n is row n.
+__constant__ int kAwqPos[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+
+MOE_DEV int awq_nib(const int32_t* packed, int64_t row, int64_t N, int64_t n) {
+    return (int)(((uint32_t)packed[row * (N / 8) + n / 8] >> (4 * kAwqPos[n % 8])) & 0xFu);
+}
+
+MOE_DEV uint8_t* awq_record(uint8_t* base, int gate_up, int64_t e, int64_t n, int64_t I, int64_t H, int64_t rec,
+                            int64_t rs, int64_t ss, int64_t* roff, int64_t* soff) {
+    if (gate_up) {
+        const int64_t r = n >= I ? 1 : 0, j = n - r * I;
+        *roff = r * rs;
+        *soff = 2 * rs + r * ss;
+        return base + (e * I + j) * rec;
+    }
+    *roff = 0;
+    *soff = rs;
+    return base + (e * H + n) * rec;
+}
+
+__global__ void awq_pack_q_kernel(uint8_t* base, const int32_t* qw, int64_t Kd, int64_t N, int gate_up, int64_t I,
+                                  int64_t H, int64_t rec, int64_t rs, int64_t ss) {
+    const int64_t e = blockIdx.y;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over n * (Kd/2)
+    if (idx >= N * (Kd / 2)) return;
+    const int64_t n = idx / (Kd / 2), kb = idx % (Kd / 2);
+    const int32_t* q = qw + e * Kd * (N / 8);
+    const int lo = awq_nib(q, 2 * kb, N, n), hi = awq_nib(q, 2 * kb + 1, N, n);
+    int64_t roff, soff;
+    uint8_t* r = awq_record(base, gate_up, e, n, I, H, rec, rs, ss, &roff, &soff);
+    r[roff + kb] = (uint8_t)(lo | (hi << 4));
+}
+
+__global__ void awq_pack_sz_kernel(uint8_t* base, const uint16_t* sc, const int32_t* qz, int64_t ng, int64_t N,
+                                   int gate_up, int64_t I, int64_t H, int64_t rec, int64_t rs, int64_t ss) {
+    const int64_t e = blockIdx.y;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // over n * ng
+    if (idx >= N * ng) return;
+    const int64_t n = idx / ng, g = idx % ng;
+    int64_t roff, soff;
+    uint8_t* r = awq_record(base, gate_up, e, n, I, H, rec, rs, ss, &roff, &soff);
+    reinterpret_cast<uint16_t*>(r + soff)[g] = sc[(e * ng + g) * N + n];
+    r[soff + 2 * ng + g] = (uint8_t)awq_nib(qz + e * ng * (N / 8), g, N, n);
 }
 
 int ensure_workspace(moe_engine* eng, int64_t positions) {
@@ -352,8 +407,11 @@ bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
     const int rpg = 32 / lpr;
     int64_t off = round_up((int64_t)(3 * TK + 5 * E + 4) * 4, 128);
     p.off_x = (int)off;
-    const int64_t xbytes = round_up((int64_t)T * H, 16) + (int64_t)T * nb1 * 8;
-    const int64_t hbytes = round_up((int64_t)TK * I, 16) + (int64_t)TK * nb2 * 8;
+    const bool awq = eng->cfg.quant_type == MOE_AWQ;
+    const int64_t xbytes = awq ? (int64_t)T * H * 2 + (int64_t)T * nb1 * 4
+                               : round_up((int64_t)T * H, 16) + (int64_t)T * nb1 * 8;
+    const int64_t hbytes = awq ? (int64_t)TK * I * 4 + (int64_t)TK * nb2 * 4
+                               : round_up((int64_t)TK * I, 16) + (int64_t)TK * nb2 * 8;
     off += round_up(std::max(xbytes, hbytes), 128);
     p.off_out = (int)off;
     p.rows_max = (H + G - 1) / G;
@@ -378,14 +436,15 @@ bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
     p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
     p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
     p.scale_bf16 = eng->scale_bf16;
+    p.group = eng->cfg.group_size;
     pl.smem = (size_t)off;
     pl.grid = G;
     return true;
 }
 
-template <bool Q4>
+template <int FMT>
 int launch_decode(const DecodePlan& pl, cudaStream_t st) {
-    auto kern = moe_decode_kernel<Q4>;
+    auto kern = moe_decode_kernel<FMT>;
     static thread_local int smem_set[64] = {};  // per device: largest opt-in already applied
     int dev = 0;
     cudaGetDevice(&dev);
@@ -438,8 +497,7 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     eng->num_sms = prop.multiProcessorCount;
     eng->max_smem = (int)prop.sharedMemPerBlockOptin;
     int rc = MOE_OK;
-    if (cfg->quant_type == MOE_AWQ) rc = awq_alloc(eng->awq, E, H, I, cfg->group_size);
-    else rc = alloc_q_layout(eng);
+    rc = alloc_q_layout(eng);
     if (rc == MOE_OK) rc = ensure_workspace(eng, 64);
     if (rc == MOE_OK && (cudaEventCreate(&eng->ev0) != cudaSuccess || cudaEventCreate(&eng->ev1) != cudaSuccess))
         rc = fail(MOE_ERR_CUDA, "cudaEventCreate failed");
@@ -456,7 +514,6 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     DeviceGuard g(eng->cfg.device);
     cudaFree(eng->gu);
     cudaFree(eng->dn);
-    awq_free(eng->awq);
     cudaFree(eng->h_ws);
     cudaFree(eng->hmax);
     cudaFree(eng->bar);
@@ -562,10 +619,26 @@ extern "C" int moe_engine_load_awq(moe_engine* eng, const void* w13_qw, const vo
     uint8_t* owned[6] = {};
     for (int i = 0; i < 6; ++i)
         if (int rc = stage_to_device(srcs[i], sizes[i], src_on_device, st, &dev[i], &owned[i])) return rc;
-    int rc = awq_pack(eng->awq, dev, st);
+    const int64_t U1 = eng->unit_bytes(), R2 = eng->row_bytes();
+    {   // gate_up: Kd = H, N = 2I
+        const int64_t N = 2 * I, n1 = N * (H / 2), n2 = N * (H / G);
+        awq_pack_q_kernel<<<dim3((unsigned)((n1 + 255) / 256), (unsigned)E), 256, 0, st>>>(
+            eng->gu, reinterpret_cast<const int32_t*>(dev[0]), H, N, 1, I, H, U1, eng->rs1, eng->ss1);
+        awq_pack_sz_kernel<<<dim3((unsigned)((n2 + 255) / 256), (unsigned)E), 256, 0, st>>>(
+            eng->gu, reinterpret_cast<const uint16_t*>(dev[1]), reinterpret_cast<const int32_t*>(dev[2]), H / G, N, 1,
+            I, H, U1, eng->rs1, eng->ss1);
+    }
+    {   // down: Kd = I, N = H
+        const int64_t N = H, n1 = N * (I / 2), n2 = N * (I / G);
+        awq_pack_q_kernel<<<dim3((unsigned)((n1 + 255) / 256), (unsigned)E), 256, 0, st>>>(
+            eng->dn, reinterpret_cast<const int32_t*>(dev[3]), I, N, 0, I, H, R2, eng->rs2, eng->ss2);
+        awq_pack_sz_kernel<<<dim3((unsigned)((n2 + 255) / 256), (unsigned)E), 256, 0, st>>>(
+            eng->dn, reinterpret_cast<const uint16_t*>(dev[4]), reinterpret_cast<const int32_t*>(dev[5]), I / G, N, 0,
+            I, H, R2, eng->rs2, eng->ss2);
+    }
+    CUDA_TRY(cudaGetLastError());
     for (int i = 0; i < 6; ++i)
-        if (owned[i]) cudaFreeAsync(owned[i], st);
-    if (rc) return fail(MOE_ERR_CUDA, std::string("AWQ pack: ") + cudaGetErrorString(cudaGetLastError()));
+        if (owned[i]) CUDA_TRY(cudaFreeAsync(owned[i], st));
     CUDA_TRY(cudaStreamSynchronize(st));
     eng->loaded = true;
     return MOE_OK;
@@ -593,17 +666,6 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     if (T == 0) return MOE_OK;
     const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
-    if (eng->cfg.quant_type == MOE_AWQ) {
-        if (int rc = ensure_workspace(eng, T * K)) return rc;
-        CUDA_TRY(cudaEventRecord(eng->ev0, st));
-        int rc = awq_forward(eng->awq, eng->num_sms, eng->max_smem, (int)eng->cfg.expert_offset, x, y, topk_ids,
-                             topk_w, (int)T, (int)K, act_dtype == MOE_BF16, out_dtype, eng->h_ws, eng->bar, eng->err,
-                             st);
-        if (rc) return fail(MOE_ERR_CUDA, std::string("AWQ forward: ") + cudaGetErrorString(cudaGetLastError()));
-        CUDA_TRY(cudaEventRecord(eng->ev1, st));
-        eng->timed = true;
-        return MOE_OK;
-    }
     // token slice that fits the decode kernel's shared-memory plan
     int64_t slice = T;
     DecodePlan pl;
@@ -630,7 +692,9 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         p.hmax = eng->hmax;
         p.hmax_stride = (int32_t)(eng->h_cap * (I / 32));
         p.dbg = eng->timeline;
-        const int rc = eng->cfg.quant_type == MOE_Q4_0 ? launch_decode<true>(pl, st) : launch_decode<false>(pl, st);
+        const int qt = eng->cfg.quant_type;
+        const int rc = qt == MOE_Q4_0 ? launch_decode<kQ4>(pl, st)
+                                      : (qt == MOE_AWQ ? launch_decode<kAWQ>(pl, st) : launch_decode<kQ8>(pl, st));
         if (rc) return rc;
     }
     if (timed) {
@@ -672,15 +736,17 @@ extern "C" int moe_engine_device_error(moe_engine* eng, int32_t* code) {
 extern "C" int moe_engine_export_expert(moe_engine* eng, int64_t expert, int32_t which, void* qs_out,
                                         void* d_out) {
     if (int rc = check_engine(eng)) return rc;
-    if (eng->cfg.quant_type == MOE_AWQ) return fail(MOE_ERR_STATE, "export is for Q8_0/Q4_0 engines");
     const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
     if (expert < 0 || expert >= E || (which != 0 && which != 1) || !qs_out || !d_out)
         return fail(MOE_ERR_INVALID, "bad export argument");
     DeviceGuard g(eng->cfg.device);
-    const bool q4 = eng->cfg.quant_type == MOE_Q4_0;
+    const bool awq = eng->cfg.quant_type == MOE_AWQ;
+    const bool q4 = eng->cfg.quant_type == MOE_Q4_0 || awq;
     const int64_t rows = which == 0 ? 2 * I : H;
-    const int64_t qrow = which == 0 ? (q4 ? H / 2 : H) : (q4 ? I / 2 : I);
-    const int64_t srow = which == 0 ? (H / 32) * 2 : (I / 32) * 2;
+    const int64_t kd = which == 0 ? H : I;
+    const int64_t qrow = q4 ? kd / 2 : kd;
+    const int64_t ng = awq ? kd / eng->cfg.group_size : kd / 32;
+    const int64_t srow = awq ? ng * 3 : ng * 2;  // AWQ: bf16 scales then u8 zeros
     const int map = which == 0 ? kGateUp : kDown;
     const uint8_t* base = which == 0 ? eng->gu + (size_t)expert * I * eng->unit_bytes()
                                      : eng->dn + (size_t)expert * H * eng->row_bytes();

@@ -1,4 +1,5 @@
-// Persistent fused MoE layer kernel for decode-size token counts (Q8_0 / Q4_0).
+// Persistent fused MoE layer kernel for decode-size token counts (Q8_0 / Q4_0 /
+// AWQ W4A16).
 //
 // One CTA per SM (cooperative launch), kWarps warps per CTA, no producer warp:
 // every warp streams its own work items with cp.async.bulk into a private ring
@@ -16,6 +17,9 @@
 //            gemm_kernels.cpp:394-425), computes the down rows [n0,n1) it owns for
 //            ALL active experts and then the k-ordered combine
 //            y[t][n] = sum_k w[t,k] out[pos(t,k)][n] (q8_gemm.cpp:593-613).
+// AWQ W4A16 keeps the activations 16-bit (no Q8_0 quantisation): a 32-block of a
+// weight row contributes s * (sum q*x - z * sum x) with the group's bf16 scale s
+// and zero z, and h stays fp32 (no requantisation, no block maxima).
 // A warp's ring is issued `slots` items ahead across the phase boundary, so the
 // down-projection weights are in flight while the CTAs wait at the grid
 // barrier.  Weights cross HBM exactly once per launch.
@@ -28,6 +32,8 @@ constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTokTile = 4;  // token rows held in registers per pass
 constexpr int kStamps = 16;
+
+enum Fmt : int { kQ8 = 0, kQ4 = 1, kAWQ = 2 };
 
 struct DecodeParams {
     // gate_up unit records [E][I]: gate qs row j (rs1) | up qs row j (rs1) | gate scales (ss1) | up scales (ss1)
@@ -51,6 +57,7 @@ struct DecodeParams {
     int32_t rows_max;       // phase-2 rows per CTA (upper bound)
     int32_t lanes_per_row;  // phase-2 lanes per down row (power of two)
     int32_t units_per_item; // phase-1 gate/up units per bulk copy (1, 2 or 4)
+    int32_t group;          // AWQ group size along K (multiple of 32)
     unsigned long long* dbg;  // optional per-CTA phase stamps [grid][kStamps] (globaltimer ns)
 };
 
@@ -254,6 +261,91 @@ MOE_DEV void requant_h_smem(const float* h, const uint32_t* hmax, int P, int I, 
     }
 }
 
+// ------------------------------------------------------------------ AWQ
+// Token rows for AWQ: the raw 16-bit values are kept and each 32-block's sum
+// (fp32) is stored beside them, one thread per block.
+MOE_DEV void stage_x_awq(const uint8_t* x, int act_bf16, int nrows, int cols, uint16_t* xr, float* xsum, int tid,
+                         int nthreads) {
+    const int nblk = nrows * (cols >> 5);
+    for (int g = tid; g < nblk; g += nthreads) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)g * 64);
+        uint4* dst = reinterpret_cast<uint4*>(xr + (size_t)g * 32);
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 r = __ldg(src + k);
+            dst[k] = r;
+            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                sum += scale_to_f32((uint16_t)(w4[i] & 0xffffu), act_bf16) + scale_to_f32((uint16_t)(w4[i] >> 16), act_bf16);
+        }
+        xsum[g] = sum;
+    }
+}
+
+// h [P][I] fp32 (global) -> shared memory with per-block sums, one thread per block.
+MOE_DEV void stage_h_awq(const float* h, int P, int I, float* hf, float* hsum, int tid) {
+    const int nblk = P * (I >> 5);
+    for (int g = tid; g < nblk; g += kThreads) {
+        const float4* src = reinterpret_cast<const float4*>(h + (size_t)g * 32);
+        float4* dst = reinterpret_cast<float4*>(hf + (size_t)g * 32);
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 f = __ldcg(src + k);
+            dst[k] = f;
+            sum += (f.x + f.y) + (f.z + f.w);
+        }
+        hsum[g] = sum;
+    }
+}
+
+MOE_DEV float nib_f(uint32_t w, int n) { return __uint_as_float(0x4B000000u | ((w >> (4 * n)) & 0xFu)) - 8388608.0f; }
+
+// sum over a 32-block of q[e] * x[e], q the sequential nibbles of `qw`, x fp32 or 16-bit.
+MOE_DEV float awq_qx_f32(const uint4 qw, const float* x) {
+    const uint32_t w4[4] = {qw.x, qw.y, qw.z, qw.w};
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 a = reinterpret_cast<const float4*>(x)[2 * i];
+        const float4 b = reinterpret_cast<const float4*>(x)[2 * i + 1];
+        acc0 = fmaf(nib_f(w4[i], 0), a.x, acc0);
+        acc1 = fmaf(nib_f(w4[i], 1), a.y, acc1);
+        acc0 = fmaf(nib_f(w4[i], 2), a.z, acc0);
+        acc1 = fmaf(nib_f(w4[i], 3), a.w, acc1);
+        acc0 = fmaf(nib_f(w4[i], 4), b.x, acc0);
+        acc1 = fmaf(nib_f(w4[i], 5), b.y, acc1);
+        acc0 = fmaf(nib_f(w4[i], 6), b.z, acc0);
+        acc1 = fmaf(nib_f(w4[i], 7), b.w, acc1);
+    }
+    return acc0 + acc1;
+}
+
+MOE_DEV float awq_qx_16(const uint4 qw, const uint16_t* x, int bf) {
+    const uint32_t w4[4] = {qw.x, qw.y, qw.z, qw.w};
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 r = reinterpret_cast<const uint4*>(x)[i];
+        const uint32_t xv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            acc0 = fmaf(nib_f(w4[i], 2 * k), scale_to_f32((uint16_t)(xv[k] & 0xffffu), bf), acc0);
+            acc1 = fmaf(nib_f(w4[i], 2 * k + 1), scale_to_f32((uint16_t)(xv[k] >> 16), bf), acc1);
+        }
+    }
+    return acc0 + acc1;
+}
+
+// Group scale (bf16) and zero (u8) of 32-block b of a row whose scale field is `sc`.
+MOE_DEV void awq_sz(const uint8_t* sc, int b, int blocks_per_group, int ngroups, float& s, float& z) {
+    const int g = b / blocks_per_group;
+    s = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(sc)[g] << 16);
+    z = (float)sc[2 * ngroups + g];
+}
+
 // Exact int32 dot of one 32-block: weights (Q8: 32 bytes, Q4: 16 bytes of
 // nibbles) against 32 int8 activations (Q4: permuted, bias 8 via asum).
 template <bool Q4>
@@ -327,13 +419,17 @@ MOE_DEV void issue_p2(const DecodeParams& p, const RouteSmem& rt, const P2Work& 
     bulk_g2s(slot, p.dn + ((size_t)rt.ue[ui] * p.H + w2.n0 + r0) * rb, rows * rb, bar);
 }
 
-template <bool Q4>
+template <int FMT>
 __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodeParams p) {
+    constexpr bool Q4 = FMT == kQ4;
+    constexpr bool AWQ = FMT == kAWQ;
+    constexpr int BB = FMT == kQ8 ? 32 : 16;  // weight bytes per 32-block
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const int TK = p.T * p.K, E = p.E, H = p.H, I = p.I;
     const int nb1 = H >> 5, nb2 = I >> 5;
+    const int bpg = AWQ ? p.group >> 5 : 1, ng1 = AWQ ? H / p.group : 0, ng2 = AWQ ? I / p.group : 0;
     unsigned long long* dbg = p.dbg ? p.dbg + (size_t)cta * kStamps : nullptr;
     if (dbg && tid == 0) { dbg[0] = global_ns(); dbg[13] = clock64(); }
 
@@ -358,7 +454,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
             if (dbg) dbg[1] = global_ns();
         }
     } else {
-        quant_x_smem<Q4>(static_cast<const uint8_t*>(p.x), p.act_bf16, p.T, H, xq, xd, xs, tid, kThreads - 32);
+        if constexpr (AWQ)
+            stage_x_awq(static_cast<const uint8_t*>(p.x), p.act_bf16, p.T, H, reinterpret_cast<uint16_t*>(xq),
+                        reinterpret_cast<float*>(xq + (size_t)p.T * H * 2), tid, kThreads - 32);
+        else
+            quant_x_smem<Q4>(static_cast<const uint8_t*>(p.x), p.act_bf16, p.T, H, xq, xd, xs, tid, kThreads - 32);
         if (dbg && tid == 0) dbg[2] = global_ns();
     }
     fence_barrier_init();
@@ -435,8 +535,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
             const uint8_t* rec = myring + (size_t)s * p.slot_bytes + (size_t)(valid ? uslot : 0) * 2 * (p.rs1 + p.ss1);
             const uint8_t* qg = rec;
             const uint8_t* qu = rec + p.rs1;
-            const uint16_t* sgate = reinterpret_cast<const uint16_t*>(rec + 2 * p.rs1);
-            const uint16_t* sup = reinterpret_cast<const uint16_t*>(rec + 2 * p.rs1 + p.ss1);
+            const uint8_t* sgate_raw = rec + 2 * p.rs1;
+            const uint8_t* sup_raw = rec + 2 * p.rs1 + p.ss1;
+            const uint16_t* sgate = reinterpret_cast<const uint16_t*>(sgate_raw);
+            const uint16_t* sup = reinterpret_cast<const uint16_t*>(sup_raw);
             const int j = j0 + uslot;
             const int ps = rt.ups[u], cnt = rt.ucnt[u];
             for (int m0 = 0; m0 < cnt; m0 += kTokTile) {  // up to kTokTile tokens per weight load
@@ -452,18 +554,36 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
                 if (valid) {
 #pragma unroll 2
                     for (int b = usub; b < nb1; b += LPU) {
-                        const uint4* wg = reinterpret_cast<const uint4*>(qg + (size_t)b * (Q4 ? 16 : 32));
-                        const uint4* wu = reinterpret_cast<const uint4*>(qu + (size_t)b * (Q4 ? 16 : 32));
-                        const float dg = scale_to_f32(sgate[b], sbf), du = scale_to_f32(sup[b], sbf);
+                        const uint4* wg = reinterpret_cast<const uint4*>(qg + (size_t)b * BB);
+                        const uint4* wu = reinterpret_cast<const uint4*>(qu + (size_t)b * BB);
+                        if constexpr (AWQ) {
+                            float sg, zg, su, zu;
+                            awq_sz(sgate_raw, b, bpg, ng1, sg, zg);
+                            awq_sz(sup_raw, b, bpg, ng1, su, zu);
+                            const uint4 qwg = wg[0], qwu = wu[0];
+                            const uint16_t* xr = reinterpret_cast<const uint16_t*>(xq);
+                            const float* xsum = reinterpret_cast<const float*>(xq + (size_t)p.T * H * 2);
 #pragma unroll
-                        for (int m = 0; m < kTokTile; ++m) {
-                            if (m >= nt) break;
-                            const int t = tk[m];
-                            const uint4* a = reinterpret_cast<const uint4*>(xq + (size_t)t * H + b * 32);
-                            const float ad = xd[t * nb1 + b];
-                            const int as = Q4 ? xs[t * nb1 + b] : 0;
-                            ag[m] += ((float)block_dot<Q4>(wg, a, as) * dg) * ad;
-                            au[m] += ((float)block_dot<Q4>(wu, a, as) * du) * ad;
+                            for (int m = 0; m < kTokTile; ++m) {
+                                if (m >= nt) break;
+                                const int t = tk[m];
+                                const uint16_t* xb = xr + (size_t)t * H + b * 32;
+                                const float sx = xsum[t * nb1 + b];
+                                ag[m] += sg * (awq_qx_16(qwg, xb, p.act_bf16) - zg * sx);
+                                au[m] += su * (awq_qx_16(qwu, xb, p.act_bf16) - zu * sx);
+                            }
+                        } else {
+                            const float dg = scale_to_f32(sgate[b], sbf), du = scale_to_f32(sup[b], sbf);
+#pragma unroll
+                            for (int m = 0; m < kTokTile; ++m) {
+                                if (m >= nt) break;
+                                const int t = tk[m];
+                                const uint4* a = reinterpret_cast<const uint4*>(xq + (size_t)t * H + b * 32);
+                                const float ad = xd[t * nb1 + b];
+                                const int as = Q4 ? xs[t * nb1 + b] : 0;
+                                ag[m] += ((float)block_dot<Q4>(wg, a, as) * dg) * ad;
+                                au[m] += ((float)block_dot<Q4>(wu, a, as) * du) * ad;
+                            }
                         }
                     }
                 }
@@ -484,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
                     const float hv = silu_mul(g, uu);
                     const int pos = ps + m0 + usub;
                     p.h_ws[(size_t)pos * I + j] = hv;
-                    atomicMax(hmax + (size_t)pos * nb2 + (j >> 5), __float_as_uint(fabsf(hv)));
+                    if constexpr (!AWQ) atomicMax(hmax + (size_t)pos * nb2 + (j >> 5), __float_as_uint(fabsf(hv)));
                 }
             }
             refill(s);
@@ -509,10 +629,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     float* hd = reinterpret_cast<float*>(hq + (size_t)P * I);
     int32_t* hs = reinterpret_cast<int32_t*>(hd + (size_t)P * nb2);
     float* outs = reinterpret_cast<float*>(smem + p.off_out);
-    if (ok && w2.R > 0 && U > 0) requant_h_smem<Q4>(p.h_ws, hmax, P, I, hq, hd, hs, tid);
+    float* hf = reinterpret_cast<float*>(smem + p.off_x);        // AWQ: fp32 h [P][I]
+    float* hsum = hf + (size_t)P * I;                              // AWQ: per-block sums
+    if (ok && w2.R > 0 && U > 0) {
+        if constexpr (AWQ) stage_h_awq(p.h_ws, P, I, hf, hsum, tid);
+        else requant_h_smem<Q4>(p.h_ws, hmax, P, I, hq, hd, hs, tid);
+    }
     {   // clear the other hmax buffer for the next launch (no CTA reads it in this launch)
         uint32_t* other = p.hmax + (size_t)(par ^ 1u) * p.hmax_stride;
-        for (int i = cta * kThreads + tid; i < p.hmax_stride; i += G * kThreads) other[i] = 0u;
+        if constexpr (!AWQ)
+            for (int i = cta * kThreads + tid; i < p.hmax_stride; i += G * kThreads) other[i] = 0u;
     }
     __syncthreads();
     if (dbg && tid == 0) dbg[9] = global_ns();
@@ -539,15 +665,27 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
             if (rv) {
 #pragma unroll 2
                 for (int b = sub; b < nb2; b += LPR) {
-                    const uint4* w = reinterpret_cast<const uint4*>(wrow + (size_t)b * (Q4 ? 16 : 32));
-                    const float dw = scale_to_f32(srw[b], sbf);
+                    const uint4* w = reinterpret_cast<const uint4*>(wrow + (size_t)b * BB);
+                    if constexpr (AWQ) {
+                        float sw, zw;
+                        awq_sz(wrow + p.rs2, b, bpg, ng2, sw, zw);
+                        const uint4 qw = w[0];
 #pragma unroll
-                    for (int m = 0; m < kTokTile; ++m) {
-                        if (m >= nt) break;
-                        const int pos = ps + m0 + m;
-                        const uint4* a = reinterpret_cast<const uint4*>(hq + (size_t)pos * I + b * 32);
-                        const int is = block_dot<Q4>(w, a, Q4 ? hs[pos * nb2 + b] : 0);
-                        acc[m] += ((float)is * dw) * hd[pos * nb2 + b];
+                        for (int m = 0; m < kTokTile; ++m) {
+                            if (m >= nt) break;
+                            const int pos = ps + m0 + m;
+                            acc[m] += sw * (awq_qx_f32(qw, hf + (size_t)pos * I + b * 32) - zw * hsum[pos * nb2 + b]);
+                        }
+                    } else {
+                        const float dw = scale_to_f32(srw[b], sbf);
+#pragma unroll
+                        for (int m = 0; m < kTokTile; ++m) {
+                            if (m >= nt) break;
+                            const int pos = ps + m0 + m;
+                            const uint4* a = reinterpret_cast<const uint4*>(hq + (size_t)pos * I + b * 32);
+                            const int is = block_dot<Q4>(w, a, Q4 ? hs[pos * nb2 + b] : 0);
+                            acc[m] += ((float)is * dw) * hd[pos * nb2 + b];
+                        }
                     }
                 }
             }

@@ -47,3 +47,23 @@ def tokens(T: int, H: int, E: int, K: int, seed: int, bf16: bool = True):
     logits = rng.standard_normal((T, E), dtype=np.float32)
     ids, w = O.topk_softmax(logits, K, True)
     return bits, xf, ids, w
+
+
+def awq_weights(E: int, H: int, I: int, G: int, seed: int):
+    """AWQ GEMM-packed weights with the BASELINE configs[2] distributions: q, z uniform in [0,15]
+    (8 per int32), bf16 scales U(0.001, 0.01)."""
+    rng = np.random.default_rng(seed)
+
+    def words(shape):
+        return rng.integers(0, 2 ** 32, size=shape, dtype=np.uint64).astype(np.uint32).view(np.int32)
+
+    def scales(shape):
+        return O.f32_to_bf16_bits(rng.uniform(0.001, 0.01, size=shape).astype(np.float32))
+
+    w13_qw = words((E, H, 2 * I // 8))
+    w13_sc = scales((E, H // G, 2 * I))
+    w13_qz = words((E, H // G, 2 * I // 8))
+    w2_qw = words((E, I, H // 8))
+    w2_sc = scales((E, I // G, H))
+    w2_qz = words((E, I // G, H // 8))
+    return w13_qw, w13_sc, w13_qz, w2_qw, w2_sc, w2_qz
