@@ -1,0 +1,79 @@
+"""Expert parallelism across the GPUs of one node (one process per GPU).
+
+Experts are placed in contiguous blocks: rank r of W holds global experts
+[r*E/W, (r+1)*E/W).  Every rank receives the full hidden states and routing
+(as in the reference's caller, which hands the same [T,H] to the engine), runs
+the fused layer over its local experts only -- ids outside the block are
+skipped exactly like invalid ids in the reference (moe_common.cpp:158,175-181)
+-- and produces an fp32 partial sum; one all-reduce over NCCL (NVLink /
+NVSwitch) adds the partials, then the result is cast to the hidden dtype.
+This replaces the reference's NUMA "TP" split (moe_infer.cpp:143-205,
+q8_gemm.cpp:621-641), whose node-0 reduction becomes the all-reduce.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import numpy as np
+
+
+def expert_partition(num_experts: int, world: int) -> List[Tuple[int, int]]:
+    """[lo, hi) of global expert ids held by each rank."""
+    if world < 1 or num_experts % world != 0:
+        raise ValueError(f"num_experts={num_experts} must be divisible by the world size {world}")
+    per = num_experts // world
+    return [(r * per, (r + 1) * per) for r in range(world)]
+
+
+def local_ids(ids: np.ndarray, lo: int, hi: int) -> np.ndarray:
+    """Global ids -> this rank's local ids, -1 for experts held elsewhere (the kernel's remap)."""
+    ids = np.asarray(ids, np.int32)
+    return np.where((ids >= lo) & (ids < hi), ids - lo, -1).astype(np.int32)
+
+
+class ExpertParallelMoE:
+    """Fused MoE layer with experts sharded over a process group.
+
+    `forward` returns the full [T, H] output on every rank.  Weight loaders take
+    the full [E, ...] tensors (host or device); each rank keeps its block.
+    """
+
+    def __init__(self, num_experts: int, hidden: int, inter: int, quant_type: int, group=None,
+                 group_size: int = 128):
+        import torch
+        import torch.distributed as dist
+
+        import moe_ascend_opt_b200  # noqa: F401  (registers torch.classes.nanovllm)
+
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.lo, self.hi = expert_partition(num_experts, self.world)[self.rank]
+        self.handle = torch.classes.nanovllm.MoEInfer(num_experts, hidden, inter, quant_type)
+        if quant_type == 2:
+            self.handle.set_group_size(group_size)
+        self.handle.set_expert_parallel(self.rank, self.world)
+
+    def load_quantized(self, gate_up_qs, gate_up_d, down_qs, down_d):
+        self.handle.store_quantized_repack(gate_up_qs, gate_up_d, down_qs, down_d)
+
+    def load_awq(self, *tensors):
+        self.handle.store_awq(*tensors)
+
+    def quantize_and_store_expert(self, e: int, proj: str, w):
+        self.handle.quantize_and_store_expert(e, proj, w)
+
+    def forward(self, hidden, topk_ids, topk_w, out: Optional[object] = None):
+        import torch
+        import torch.distributed as dist
+
+        if self.world == 1:
+            y = torch.ops.nanovllm.moe_forward(hidden, topk_ids, topk_w, self.handle)
+        else:
+            part = torch.ops.nanovllm.moe_forward_partial(hidden, topk_ids, topk_w, self.handle)
+            dist.all_reduce(part, group=self.group)
+            y = part.to(hidden.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y

@@ -1,6 +1,8 @@
 """Seeded synthetic inputs and parity metrics shared by the tests."""
 from __future__ import annotations
 
+import hashlib
+
 import numpy as np
 
 from oracle import oracle as O
@@ -67,3 +69,30 @@ def awq_weights(E: int, H: int, I: int, G: int, seed: int):
     w2_sc = scales((E, I // G, H))
     w2_qz = words((E, I // G, H // 8))
     return w13_qw, w13_sc, w13_qz, w2_qw, w2_sc, w2_qz
+
+
+def expert_weights_fp32(e, seed, H, I):
+    """fp32 N(0, 0.02^2) weights of expert e (independent stream per expert)."""
+    rng = np.random.default_rng(seed * 100003 + e)
+    wg = (rng.standard_normal((I, H), dtype=np.float32) * 0.02).astype(np.float32)
+    wu = (rng.standard_normal((I, H), dtype=np.float32) * 0.02).astype(np.float32)
+    wd = (rng.standard_normal((H, I), dtype=np.float32) * 0.02).astype(np.float32)
+    return wg, wu, wd
+
+
+def big_case_inputs(T, seed, H=2048, E=128, K=8):
+    """Tokens of the full-size configs: bf16 N(0,1) hidden, softmax-top-K routing of N(0,1) logits."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, H), dtype=np.float32)
+    xb = O.f32_to_bf16_bits(x)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    ids, w = O.topk_softmax(logits, K, True)
+    return xb, ids, w
+
+
+def digest_inputs(*arrays) -> str:
+    """SHA-256 over the raw bytes of the generated inputs (checks generator stability)."""
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()

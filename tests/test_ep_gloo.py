@@ -1,0 +1,96 @@
+"""Expert-parallel decomposition on CPU ranks (gloo, world size 2).
+
+Each rank evaluates the oracle over its block of experts with the ids remapped
+the way the kernel remaps them (others -> -1), the fp32 partials are summed by
+an all-reduce, and the result must equal the single-rank forward.  This is the
+host-side contract the GPU path follows with NCCL.  A second test checks that a
+rank that fails before the collective makes its peer's collective fail instead
+of hanging (short process-group timeout)."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from moe_ascend_opt_b200.ep import expert_partition, local_ids
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, qt, result_q):
+    from oracle import oracle as O
+    from tests.helpers import q_weights, tokens
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    E, H, I, T, K = 16, 256, 128, 5, 8
+    gq, gd, dq, dd = q_weights(qt, E, H, I, 31)
+    _, xf, ids, w = tokens(T, H, E, K, 31)
+    lo, hi = expert_partition(E, world)[rank]
+    part = O.moe_forward_q(qt, False, xf, local_ids(ids, lo, hi), w, gq[lo:hi], gd[lo:hi], dq[lo:hi], dd[lo:hi])
+    t = torch.from_numpy(part)
+    dist.all_reduce(t)
+    if rank == 0:
+        full = O.moe_forward_q(qt, False, xf, ids, w, gq, gd, dq, dd)
+        result_q.put(float(np.abs(t.numpy() - full).max() / np.abs(full).max()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("qt", [0, 1])
+def test_ep_partials_sum_to_full_forward(qt):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, qt, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs)
+    assert q.get(timeout=5) < 1e-5
+
+
+def _failing_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # this rank dies between steps, before the combine
+    t = torch.ones(4)
+    try:
+        dist.all_reduce(t)
+        result_q.put("completed")
+    except Exception as ex:  # the survivor learns of it from the collective, it does not hang
+        result_q.put("error:" + type(ex).__name__)
+
+
+def test_dead_rank_fails_collective_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+    assert procs[1].exitcode == 3
+    assert q.get(timeout=5).startswith("error:")
+
+
+def test_partition_and_remap():
+    assert expert_partition(128, 8)[3] == (48, 64)
+    with pytest.raises(ValueError):
+        expert_partition(10, 4)
+    ids = np.array([[0, 5, 9, -1, 16]], np.int32)
+    assert local_ids(ids, 4, 12).tolist() == [[-1, 1, 5, -1, -1]]
