@@ -139,6 +139,21 @@ int moe_quantize_rows_q8_0(const void* x, int32_t dtype, int64_t rows, int64_t c
 int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64_t* out, int32_t max_entries,
                               int32_t* n_entries);
 
+/* Forward that allocates nothing (no counterpart in the reference).  For callers that may
+ * not call cudaMalloc when they run the layer -- serving runtimes that reserve the whole
+ * device memory at start-up and forbid later allocations, or latency-critical paths that
+ * cannot afford an allocation's implicit device synchronisation.  Same arguments and result
+ * as moe_engine_forward, on an engine whose weights are loaded; its scratch comes from a
+ * fixed 512 KiB array in device memory that every GPU loading this library holds until the
+ * process exits.  Limit: 256 + 8*T*K*(I/32) + 4*T*K*I bytes must fit in 512 KiB (e.g. T*K <=
+ * 160 at I = 768) and T must fit one decode launch; larger calls fail with MOE_ERR_INVALID.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  All calls share the one array: calls
+ * that overlap on the GPU (other streams, other threads) race and must be serialised. */
+int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* y, const int32_t* topk_ids,
+                               const float* topk_w, int64_t num_tokens, int64_t top_k,
+                               int32_t act_dtype, int32_t out_dtype, void* stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* moe_last_error(void);
 

@@ -21,7 +21,7 @@ SYMBOLS = [
     "moe_engine_create", "moe_engine_destroy", "moe_engine_load_quantized", "moe_engine_quantize_store_expert",
     "moe_engine_load_awq", "moe_engine_forward", "moe_engine_reserve", "moe_engine_last_time_ms",
     "moe_engine_device_error", "moe_engine_export_expert", "moe_route_topk", "moe_route_permute",
-    "moe_quantize_rows_q8_0", "moe_engine_debug_timeline", "moe_last_error",
+    "moe_quantize_rows_q8_0", "moe_engine_debug_timeline", "moe_engine_forward_noalloc", "moe_last_error",
 ]
 
 
@@ -65,6 +65,7 @@ def lib() -> C.CDLL:
             "moe_route_permute": [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P],
             "moe_quantize_rows_q8_0": [_P, _I32, _I64, _I64, _P, _P, _P],
             "moe_engine_debug_timeline": [_P, _I32, _P, _I32, C.POINTER(_I32)],
+            "moe_engine_forward_noalloc": [_P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _P],
         }
         for name, args in sig.items():
             f = getattr(L, name)
@@ -114,6 +115,10 @@ class Engine:
 
     def forward(self, x, y, ids, w, act_dtype, out_dtype, stream=None):
         call("moe_engine_forward", self.h, x.data_ptr(), y.data_ptr(), ids.data_ptr(), w.data_ptr(),
+             x.shape[0], ids.shape[1], act_dtype, out_dtype, stream_handle(stream))
+
+    def forward_noalloc(self, x, y, ids, w, act_dtype, out_dtype, stream=None):
+        call("moe_engine_forward_noalloc", self.h, x.data_ptr(), y.data_ptr(), ids.data_ptr(), w.data_ptr(),
              x.shape[0], ids.shape[1], act_dtype, out_dtype, stream_handle(stream))
 
     def reserve(self, T, K):

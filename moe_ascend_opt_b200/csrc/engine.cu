@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -833,4 +834,87 @@ extern "C" int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64
         CUDA_TRY(cudaMemcpy(out, eng->timeline, (size_t)n * 8, cudaMemcpyDeviceToHost));
     }
     return MOE_OK;
+}
+
+// ============================================================ no-allocation forward
+// Some callers cannot call cudaMalloc at the moment they run the layer: serving
+// runtimes that reserve all device memory up front and forbid allocations
+// afterwards, or latency-critical paths where an allocation (which may
+// synchronise the device) is not acceptable.  moe_engine_forward_noalloc runs the
+// same fused decode kernel as moe_engine_forward but takes its scratch (the h
+// workspace, the per-block maxima, the grid-barrier counter and the error word)
+// from the fixed device array below instead of the engine's workspace, so it
+// allocates nothing.  The array lives in every GPU that loads this library until
+// the process exits.
+constexpr size_t kNoAllocScratchBytes = 512 * 1024;
+constexpr size_t kNoAllocHeader = 256;  // barrier counter at 0, error word at 64
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[128] = {};
+
+// Device address of g_noalloc_scratch on `dev` (current).  In host code the array's
+// name only stands in for the symbol, so its address must be asked for once per device.
+int noalloc_scratch(int dev, unsigned char** out) {
+    if (dev < 0 || dev >= 128) return fail(MOE_ERR_INVALID, "device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return fail(MOE_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = static_cast<unsigned char*>(g_noalloc_ptr[dev]);
+    return MOE_OK;
+}
+}  // namespace
+
+extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* y, const int32_t* topk_ids,
+                                          const float* topk_w, int64_t T, int64_t K, int32_t act_dtype,
+                                          int32_t out_dtype, void* stream) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!eng->loaded) return fail(MOE_ERR_STATE, "no weights loaded");
+    if (T < 0 || K <= 0 || K > 64) return fail(MOE_ERR_INVALID, "num_tokens must be >= 0 and 1 <= top_k <= 64");
+    if (act_dtype != MOE_F16 && act_dtype != MOE_BF16) return fail(MOE_ERR_INVALID, "hidden must be f16 or bf16");
+    if (out_dtype != MOE_F16 && out_dtype != MOE_BF16 && out_dtype != MOE_F32)
+        return fail(MOE_ERR_INVALID, "bad output dtype");
+    if (T > 0 && (!x || !y || !topk_ids || !topk_w)) return fail(MOE_ERR_INVALID, "null tensor pointer");
+    const int64_t I = eng->cfg.intermediate_size;
+    const int64_t P = T * K;
+    const int64_t hm_entries = P * (I / 32);
+    const size_t need = kNoAllocHeader + (size_t)2 * hm_entries * 4 + (size_t)P * I * 4;
+    if (need > kNoAllocScratchBytes)
+        return fail(MOE_ERR_INVALID, "num_tokens x top_k x intermediate_size needs " + std::to_string(need) +
+                                         " bytes of scratch; moe_engine_forward_noalloc holds at most " +
+                                         std::to_string(kNoAllocScratchBytes));
+    DeviceGuard g(eng->cfg.device);
+    if (T == 0) return MOE_OK;
+    DecodePlan pl;
+    if (!plan_decode(eng, (int)T, (int)K, pl))
+        return fail(MOE_ERR_INVALID, "num_tokens x top_k too large for one decode launch; use moe_engine_forward");
+    unsigned char* base = nullptr;
+    if (int rc = noalloc_scratch(eng->cfg.device, &base)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // every call reuses the array: clear the barrier counter, the error word and both
+    // block-maxima buffers (they must start at zero), leave h to be overwritten
+    CUDA_TRY(cudaMemsetAsync(base, 0, kNoAllocHeader + (size_t)2 * hm_entries * 4, st));
+    DecodeParams& p = pl.p;
+    p.act_bf16 = act_dtype == MOE_BF16;
+    p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+    p.x = x;
+    p.y = y;
+    p.ids = topk_ids;
+    p.tw = topk_w;
+    p.gu = eng->gu;
+    p.dn = eng->dn;
+    p.bar = reinterpret_cast<unsigned long long*>(base);
+    p.err = reinterpret_cast<int32_t*>(base + 64);
+    p.hmax = reinterpret_cast<uint32_t*>(base + kNoAllocHeader);
+    p.hmax_stride = (int32_t)hm_entries;
+    p.h_ws = reinterpret_cast<float*>(base + kNoAllocHeader + (size_t)2 * hm_entries * 4);
+    p.dbg = nullptr;
+    const int qt = eng->cfg.quant_type;
+    return qt == MOE_Q4_0 ? launch_decode<kQ4>(pl, st)
+                          : (qt == MOE_AWQ ? launch_decode<kAWQ>(pl, st) : launch_decode<kQ8>(pl, st));
 }
