@@ -469,26 +469,28 @@ def sweep(handles, dev, args):
     res = {}
     g = torch.Generator(device=dev)
     g.manual_seed(11)
-    for T in (1, 4, 8, 32):
+    for T in (1, 4, 8, 32, 128, 1024, 4096):
+        nrot = 16 if T <= 32 else 4
         xs, ids_l, w_l, nb = [], [], [], []
-        for i in range(16):
+        for i in range(nrot):
             xs.append(torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16))
             ids, w = torch.ops.nanovllm.moe_route(torch.randn((T, E), generator=g, device=dev), K, True)
             ids_l.append(ids); w_l.append(w); nb.append(int(torch.unique(ids).numel()) * Q4_BYTES_PER_EXPERT)
-        n = 200
-        for i in range(5):
-            torch.ops.nanovllm.moe_forward(xs[i % 16], ids_l[i % 16], w_l[i % 16], handles[i % len(handles)])
+        n = 200 if T <= 32 else (40 if T <= 1024 else 10)
+        for i in range(3):
+            torch.ops.nanovllm.moe_forward(xs[i % nrot], ids_l[i % nrot], w_l[i % nrot], handles[i % len(handles)])
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
         for i in range(n):
-            torch.ops.nanovllm.moe_forward(xs[i % 16], ids_l[i % 16], w_l[i % 16], handles[i % len(handles)])
+            torch.ops.nanovllm.moe_forward(xs[i % nrot], ids_l[i % nrot], w_l[i % nrot], handles[i % len(handles)])
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / n
-        b = sum(nb[i % 16] for i in range(n)) / n
+        b = sum(nb[i % nrot] for i in range(n)) / n
         res[f"T{T}"] = {"us": round(ms * 1e3, 2), "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
+                        "TFLOP/s": round(6.0 * T * K * H * I / (ms * 1e-3) / 1e12, 2),
                         "active_experts": round(b / Q4_BYTES_PER_EXPERT, 1)}
     return res
 

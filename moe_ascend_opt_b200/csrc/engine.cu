@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <mutex>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -13,6 +14,7 @@
 #include "../../include/moe_b200.h"
 #include "common.cuh"
 #include "moe_decode.cuh"
+#include "moe_gemm.cuh"
 
 using namespace moe;
 
@@ -59,6 +61,10 @@ struct moe_engine {
     int32_t* err = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     bool timed = false;
+    int64_t gemm_min_tokens = 32;  // forwards with more tokens take the grouped-GEMM path
+    // grouped-GEMM path workspace (one allocation, carved per call)
+    uint8_t* gws = nullptr;
+    size_t gws_bytes = 0;
     unsigned long long* timeline = nullptr;  // per-CTA phase stamps when enabled
     int timeline_ctas = 0;
 };
@@ -469,6 +475,127 @@ int launch_decode(const DecodePlan& pl, cudaStream_t st) {
 
 }  // namespace
 
+// ------------------------------------------------------------------ grouped-GEMM path
+// Large token counts: parallel routing, Q8_0 token rows, two grouped GEMMs on the
+// int8 tensor cores, combine.  Only Q8_0 / Q4_0 with 2I and H multiples of 128.
+bool gemm_path_ok(const moe_engine* eng) {
+    const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    return eng->cfg.quant_type != MOE_AWQ && (2 * I) % gemm::kBN == 0 && H % gemm::kBN == 0 &&
+           eng->cfg.num_experts <= 1024;
+}
+
+struct GemmWs {
+    int32_t *blk, *counts, *starts, *mtile, *smap, *tokmap;
+    int8_t *xq, *hq;
+    float *xd, *hd, *out;
+    int32_t *xs, *hs;
+};
+
+int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    const int64_t TK = T * K, nblk = (TK + gemm::kChunk - 1) / gemm::kChunk;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off += (bytes + 255) / 256 * 256; return o; };
+    const size_t o_blk = take(nblk * E * 4), o_cnt = take(E * 4), o_st = take((E + 1) * 4), o_mt = take((E + 1) * 4);
+    const size_t o_smap = take(TK * 4), o_tok = take(TK * 4);
+    const size_t o_xq = take(T * H), o_xd = take(T * (H / 32) * 4), o_xs = take(T * (H / 32) * 4);
+    const size_t o_hq = take(TK * I), o_hd = take(TK * (I / 32) * 4), o_hs = take(TK * (I / 32) * 4);
+    const size_t o_out = take(TK * H * 4);
+    if (off > eng->gws_bytes) {
+        CUDA_TRY(cudaDeviceSynchronize());
+        if (eng->gws) CUDA_TRY(cudaFree(eng->gws));
+        eng->gws = nullptr;
+        size_t cap = std::max(off, eng->gws_bytes * 2);
+        CUDA_TRY(cudaMalloc(&eng->gws, cap));
+        eng->gws_bytes = cap;
+    }
+    uint8_t* b = eng->gws;
+    w.blk = reinterpret_cast<int32_t*>(b + o_blk);
+    w.counts = reinterpret_cast<int32_t*>(b + o_cnt);
+    w.starts = reinterpret_cast<int32_t*>(b + o_st);
+    w.mtile = reinterpret_cast<int32_t*>(b + o_mt);
+    w.smap = reinterpret_cast<int32_t*>(b + o_smap);
+    w.tokmap = reinterpret_cast<int32_t*>(b + o_tok);
+    w.xq = reinterpret_cast<int8_t*>(b + o_xq);
+    w.xd = reinterpret_cast<float*>(b + o_xd);
+    w.xs = reinterpret_cast<int32_t*>(b + o_xs);
+    w.hq = reinterpret_cast<int8_t*>(b + o_hq);
+    w.hd = reinterpret_cast<float*>(b + o_hd);
+    w.hs = reinterpret_cast<int32_t*>(b + o_hs);
+    w.out = reinterpret_cast<float*>(b + o_out);
+    return MOE_OK;
+}
+
+template <bool Q4>
+int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, const float* tw, int64_t T, int64_t K,
+                   int act_bf16, int out_kind, cudaStream_t st) {
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    const int TK = (int)(T * K);
+    GemmWs w;
+    if (int rc = gemm_workspace(eng, T, K, w)) return rc;
+    const int nblk = (TK + gemm::kChunk - 1) / gemm::kChunk;
+    const int eoff = eng->cfg.expert_offset;
+    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk);
+    gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
+                                                                                  w.mtile);
+    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk, w.starts, w.smap, w.tokmap);
+    {
+        const int nb = (int)(T * (H / 32));
+        gemm::quant_rows_kernel<Q4><<<std::min((nb + 255) / 256, eng->num_sms * 8), 256, 0, st>>>(
+            static_cast<const uint8_t*>(x), act_bf16, (int)T, H, w.xq, w.xd, w.xs);
+    }
+    CUDA_TRY(cudaGetLastError());
+    using S = gemm::Stage<Q4>;
+    const int smem = std::max(gemm::kStages * S::kBytes, gemm::kBM * (gemm::kBN / 2 + 1) * 4);
+    static thread_local int smem_set[2][2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t mt_bound = (TK + gemm::kBM - 1) / gemm::kBM + std::min(E, TK);
+    gemm::GemmParams gp{};
+    gp.scale_bf16 = eng->scale_bf16;
+    gp.counts = w.counts;
+    gp.starts = w.starts;
+    gp.mtile_start = w.mtile;
+    gp.tokmap = w.tokmap;
+    gp.topk = (int)K;
+    gp.E = E;
+    {   // gate_up: A = token rows, B = unit records (2 rows each)
+        auto kern = gemm::grouped_gemm_kernel<Q4, true>;
+        if (dev < 64 && smem_set[Q4][1][dev] < smem) {
+            CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            smem_set[Q4][1][dev] = smem;
+        }
+        gemm::GemmParams g1 = gp;
+        g1.aq = w.xq; g1.ad = w.xd; g1.as = w.xs;
+        g1.wbase = eng->gu; g1.rec = eng->unit_bytes(); g1.rows_per_rec = 2; g1.rs = eng->rs1;
+        g1.sc_off = 2 * eng->rs1; g1.ss = eng->ss1; g1.nrec = I; g1.K = H; g1.N = 2 * I;
+        g1.hq = w.hq; g1.hd = w.hd; g1.hs = w.hs;
+        kern<<<(unsigned)(mt_bound * (2 * I / gemm::kBN)), gemm::kThreads, smem, st>>>(g1);
+        CUDA_TRY(cudaGetLastError());
+    }
+    {   // down: A = requantised h rows, B = down row records
+        auto kern = gemm::grouped_gemm_kernel<Q4, false>;
+        if (dev < 64 && smem_set[Q4][0][dev] < smem) {
+            CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            smem_set[Q4][0][dev] = smem;
+        }
+        gemm::GemmParams g2 = gp;
+        g2.aq = w.hq; g2.ad = w.hd; g2.as = w.hs;
+        g2.wbase = eng->dn; g2.rec = eng->row_bytes(); g2.rows_per_rec = 1; g2.rs = eng->rs2;
+        g2.sc_off = eng->rs2; g2.ss = eng->ss2; g2.nrec = H; g2.K = I; g2.N = H;
+        g2.out = w.out;
+        kern<<<(unsigned)(mt_bound * (H / gemm::kBN)), gemm::kThreads, smem, st>>>(g2);
+        CUDA_TRY(cudaGetLastError());
+    }
+    {
+        const int64_t total = T * (H / 4);
+        gemm::combine_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, eng->num_sms * 16), 256, 0, st>>>(
+            w.out, w.smap, tw, (int)T, (int)K, H, y, out_kind);
+        CUDA_TRY(cudaGetLastError());
+    }
+    return MOE_OK;
+}
+
 // =================================================================== C ABI
 extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (!cfg || !out) return fail(MOE_ERR_INVALID, "null argument");
@@ -496,6 +623,7 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
         return fail(MOE_ERR_CUDA, "cudaGetDeviceProperties failed");
     }
     eng->num_sms = prop.multiProcessorCount;
+    if (const char* v = std::getenv("MOE_GEMM_MIN_TOKENS")) eng->gemm_min_tokens = std::atoll(v);
     eng->max_smem = (int)prop.sharedMemPerBlockOptin;
     int rc = MOE_OK;
     rc = alloc_q_layout(eng);
@@ -519,6 +647,7 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     cudaFree(eng->hmax);
     cudaFree(eng->bar);
     cudaFree(eng->timeline);
+    cudaFree(eng->gws);
     if (eng->ev0) cudaEventDestroy(eng->ev0);
     if (eng->ev1) cudaEventDestroy(eng->ev1);
     delete eng;
@@ -667,6 +796,22 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     if (T == 0) return MOE_OK;
     const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
+    if (T > eng->gemm_min_tokens && gemm_path_ok(eng)) {  // dense enough for the grouped GEMMs
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        CUDA_TRY(cudaStreamIsCapturing(st, &cap));
+        const bool timed = cap == cudaStreamCaptureStatusNone;
+        if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
+        const int okind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+        const int rc = eng->cfg.quant_type == MOE_Q4_0
+                           ? forward_gemm_t<true>(eng, x, y, topk_ids, topk_w, T, K, act_dtype == MOE_BF16, okind, st)
+                           : forward_gemm_t<false>(eng, x, y, topk_ids, topk_w, T, K, act_dtype == MOE_BF16, okind, st);
+        if (rc) return rc;
+        if (timed) {
+            CUDA_TRY(cudaEventRecord(eng->ev1, st));
+            eng->timed = true;
+        }
+        return MOE_OK;
+    }
     // token slice that fits the decode kernel's shared-memory plan
     int64_t slice = T;
     DecodePlan pl;
@@ -824,6 +969,7 @@ extern "C" int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64
     if (!enable && eng->timeline) {
         CUDA_TRY(cudaDeviceSynchronize());
         cudaFree(eng->timeline);
+    cudaFree(eng->gws);
         eng->timeline = nullptr;
         eng->timeline_ctas = 0;
     }

@@ -1,0 +1,518 @@
+// Grouped-GEMM path of the fused MoE layer for large token counts (Q8_0 / Q4_0).
+//
+// Per launch sequence (all stream ordered):
+//   route_count / route_scan / route_place  parallel stable counting sort of the
+//        T*K pairs by expert (moe_common.cpp:146-184): counts, starts, positions in
+//        (t,k) order, plus per-expert tile offsets for the GEMMs;
+//   quant_rows (gemm_kernels.cpp:25-58)     token rows -> Q8_0, in the weight's
+//        activation byte order;
+//   gemm_gate_up                            per (expert, 64-token tile, 64-unit tile):
+//        C = A x W^T over the expert's gathered token rows with int8 tensor-core
+//        MMAs, one MMA per 32-block and the reference's per-block fold
+//        c += (f32(isum) * d_w) * d_a in fp32 registers; epilogue SiLU(gate)*up and
+//        the Q8_0 requant of h per 32-unit block (pack_A_q8_0, gemm_kernels.cpp:394-425)
+//        -- the tile holds whole blocks, so no cross-CTA step;
+//   gemm_down                               out[pos][n] = h_q[pos] . W2[n] (fp32);
+//   combine                                 y[t] = sum_k w[t,k] out[pos(t,k)] in k
+//        order (q8_gemm.cpp:593-613), cast (q8_gemm.cpp:636-639).
+// Tensor-core instruction: mma.sync m16n8k32 (s8 x s8, or s8 x u8 for Q4_0 nibbles
+// with the -8 bias removed through the activation block sums).  A 32-block of K is
+// exactly one MMA, so the per-block integer dot needs no extra work.
+#pragma once
+#include "common.cuh"
+
+namespace moe {
+namespace gemm {
+
+constexpr int kBM = 64;        // token rows per CTA tile
+constexpr int kBN = 128;       // weight rows per CTA tile (gate_up: 64 units x 2 rows)
+constexpr int kKB = 4;         // 32-blocks per pipeline stage (K = 128)
+constexpr int kStages = 3;
+constexpr int kThreads = 256;  // 8 warps: 2 (M) x 4 (N), 32 x 32 each
+constexpr int kRowPad = 16;    // smem row padding (bank-conflict-free fragment loads)
+
+// ------------------------------------------------------------------ routing
+// Pairs are processed in chunks of kChunk by one CTA each.
+constexpr int kChunk = 1024;
+
+__global__ void route_count_kernel(const int32_t* ids, int TK, int E, int e_off, int32_t* blk_cnt) {
+    extern __shared__ int32_t sh[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
+    __syncthreads();
+    const int base = blockIdx.x * kChunk;
+    for (int i = threadIdx.x; i < kChunk && base + i < TK; i += blockDim.x) {
+        const int g = ids[base + i] - e_off;
+        if (g >= 0 && g < E) atomicAdd(&sh[g], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) blk_cnt[(size_t)blockIdx.x * E + e] = sh[e];
+}
+
+// One CTA of >= E threads: per-block offsets (expert-major), counts, starts, and
+// per-expert first tile index of the gate_up / down GEMM tile lists.
+__global__ void route_scan_kernel(int32_t* blk_cnt, int nblk, int E, int32_t* counts, int32_t* starts,
+                                  int32_t* mtile_start) {
+    extern __shared__ int32_t sh[];  // [2][E]
+    const int e = threadIdx.x;
+    int tot = 0;
+    if (e < E) {
+        for (int b = 0; b < nblk; ++b) {
+            const int c = blk_cnt[(size_t)b * E + e];
+            blk_cnt[(size_t)b * E + e] = tot;  // exclusive offset of block b within expert e
+            tot += c;
+        }
+        sh[e] = tot;
+        sh[E + e] = (tot + kBM - 1) / kBM;
+    }
+    __syncthreads();
+    if (e == 0) {  // serial scan over experts (E <= a few hundred)
+        int run = 0, trun = 0;
+        for (int k = 0; k < E; ++k) {
+            const int c = sh[k], t = sh[E + k];
+            counts[k] = c;
+            starts[k] = run;
+            mtile_start[k] = trun;
+            run += c;
+            trun += t;
+        }
+        starts[E] = run;
+        mtile_start[E] = trun;
+    }
+}
+
+// Stable positions: warp 0 walks the chunk 32 pairs at a time in (t,k) order.
+__global__ void route_place_kernel(const int32_t* ids, int TK, int E, int e_off, const int32_t* blk_off,
+                                   const int32_t* starts, int32_t* smap, int32_t* tokmap) {
+    extern __shared__ int32_t run[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = starts[e] + blk_off[(size_t)blockIdx.x * E + e];
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    const int base = blockIdx.x * kChunk;
+    for (int i0 = 0; i0 < kChunk && base + i0 < TK; i0 += 32) {
+        const int i = base + i0 + lane;
+        int e = -1;
+        if (i < TK) {
+            const int g = ids[i] - e_off;
+            e = (g >= 0 && g < E) ? g : -1;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        int b = 0;
+        if (e >= 0) b = run[e];
+        __syncwarp();
+        if (i < TK) {
+            const int pos = e >= 0 ? b + rank : -1;
+            smap[i] = pos;
+            if (pos >= 0) tokmap[pos] = i;
+        }
+        if (e >= 0 && rank == 0) run[e] = b + __popc(peers);
+        __syncwarp();
+    }
+}
+
+// Token rows -> Q8_0 (thread per 32-block), bytes in the weight format's order.
+template <bool Q4>
+__global__ void quant_rows_kernel(const uint8_t* x, int act_bf16, int rows, int cols, int8_t* q, float* d,
+                                  int32_t* s) {
+    const int nblk = rows * (cols >> 5);
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < nblk; g += gridDim.x * blockDim.x) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)g * 64);
+        float v[32];
+        float amax = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 r = __ldg(src + k);
+            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[8 * k + 2 * i] = scale_to_f32((uint16_t)(w4[i] & 0xffffu), act_bf16);
+                v[8 * k + 2 * i + 1] = scale_to_f32((uint16_t)(w4[i] >> 16), act_bf16);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        const float dd = q8_scale(amax);
+        const float id = q8_inv(dd);
+        int qv[32];
+        int sum = 0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            qv[e] = q8_quant(v[e], id);
+            sum += qv[e];
+        }
+        uint32_t wv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int e = Q4 ? 8 * (k >> 1) + (k & 1) + 2 * i : 4 * k + i;
+                w |= (uint32_t)(qv[e] & 0xff) << (8 * i);
+            }
+            wv[k] = w;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(q + (size_t)g * 32);
+        dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+        d[g] = dd;
+        if (Q4) s[g] = sum;
+    }
+}
+
+// ------------------------------------------------------------------ MMA helpers
+template <bool BU8>
+MOE_DEV void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    if (BU8)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0), "r"(0), "r"(0), "r"(0));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+MOE_DEV void cp_async16(void* smem_dst, const void* gsrc, bool pred) {
+    const uint32_t d = smem_u32(smem_dst);
+    const int sz = pred ? 16 : 0;  // zero-fill when the source row does not exist
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gsrc), "r"(sz) : "memory");
+}
+MOE_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MOE_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// ------------------------------------------------------------------ grouped GEMM
+struct GemmParams {
+    // A: quantised activation rows (gate_up: token rows [T][K], gathered through
+    // tokmap/K; down: position rows [P][K]) with per-block scales (and Q4 sums)
+    const int8_t* aq;
+    const float* ad;
+    const int32_t* as;
+    // B: weight records; row n of expert e at wbase + (e*nrec + n/rows_per_rec)*rec + (n%rows_per_rec)*rs
+    const uint8_t* wbase;
+    int64_t rec;        // record bytes
+    int rows_per_rec;   // gate_up: 2 (gate, up), down: 1
+    int rs;             // bytes of one row's quants inside a record
+    int sc_off;         // byte offset of the scale field of row 0 inside a record
+    int ss;             // bytes of one row's scale field
+    int nrec;           // records per expert (gate_up: I units, down: H rows)
+    int K;              // reduction length (elements)
+    int N;              // output columns per expert (gate_up: 2I, down: H)
+    int scale_bf16;
+    const int32_t* counts;
+    const int32_t* starts;
+    const int32_t* mtile_start;  // [E+1] first m-tile of each expert
+    const int32_t* tokmap;       // gate_up: pair index per position (token = pair / topk)
+    int topk;
+    int E;
+    // outputs
+    int8_t* hq;   // gate_up: requantised h [P][I]
+    float* hd;    // [P][I/32]
+    int32_t* hs;  // [P][I/32] (Q4)
+    float* out;   // down: [P][H]
+};
+
+// Shared-memory layout of one stage.
+template <bool Q4>
+struct Stage {
+    static constexpr int kAKB = kKB * 32;               // activation bytes per row per stage
+    static constexpr int kARow = kAKB + kRowPad;
+    static constexpr int kBKB = kKB * (Q4 ? 16 : 32);  // weight bytes per row per stage
+    static constexpr int kBRow = kBKB + kRowPad;
+    static constexpr int kA = kBM * kARow;
+    static constexpr int kB = kBN * kBRow;
+    static constexpr int kAd = kBM * kKB * 4;
+    static constexpr int kAs = kBM * kKB * 4;
+    static constexpr int kBd = kBN * kKB * 2;
+    static constexpr int kBytes = kA + kB + kAd + kAs + kBd;
+};
+
+template <bool Q4, bool GATE_UP>
+__global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams p) {
+    using S = Stage<Q4>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = warp >> 2, wn = warp & 3;  // warp tile: rows wm*32.., cols wn*32..
+    const int g = lane >> 2, c = lane & 3;
+
+    // ---- tile -> (expert, m tile, n tile)
+    const int ntiles_n = p.N / kBN;
+    const int mt_total = p.mtile_start[p.E];
+    const int tile = blockIdx.x;
+    if (tile >= mt_total * ntiles_n) return;
+    const int mt_glob = tile / ntiles_n, nt = tile % ntiles_n;
+    int lo = 0, hi = p.E;  // expert e with mtile_start[e] <= mt_glob < mtile_start[e+1]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (p.mtile_start[mid] <= mt_glob) lo = mid;
+        else hi = mid;
+    }
+    const int e = lo;
+    const int m0 = (mt_glob - p.mtile_start[e]) * kBM;
+    const int cnt = p.counts[e];
+    const int pos0 = p.starts[e] + m0;
+    const int mrows = min(kBM, cnt - m0);
+    const int n0 = nt * kBN;
+    const int nkb = p.K / 32;
+
+    // per-row source pointers (loader threads)
+    // A: 64 rows x (kKB*32) bytes per stage = 64 x 8 chunks of 16 B -> 2 chunks per thread
+    // B: 128 rows x kBKB bytes -> (Q4: 4 chunks, Q8: 8 chunks per row)
+    auto a_row_ptr = [&](int r) -> int64_t {  // element offset of row r (clamped)
+        const int rr = min(r, mrows - 1);
+        const int pos = pos0 + rr;
+        const int64_t row = GATE_UP ? (int64_t)(p.tokmap[pos] / p.topk) : (int64_t)pos;
+        return row;
+    };
+    auto b_row_addr = [&](int n) -> const uint8_t* {
+        const int gn = n0 + n;
+        const int rec = gn / p.rows_per_rec, sub = gn % p.rows_per_rec;
+        return p.wbase + ((int64_t)e * p.nrec + rec) * p.rec + (int64_t)sub * p.rs;
+    };
+    auto b_scale_addr = [&](int n) -> const uint16_t* {
+        const int gn = n0 + n;
+        const int rec = gn / p.rows_per_rec, sub = gn % p.rows_per_rec;
+        return reinterpret_cast<const uint16_t*>(p.wbase + ((int64_t)e * p.nrec + rec) * p.rec + p.sc_off +
+                                                 (int64_t)sub * p.ss);
+    };
+
+    auto load_stage = [&](int st, int kb0) {
+        uint8_t* base = smem + (size_t)st * S::kBytes;
+        int8_t* sA = reinterpret_cast<int8_t*>(base);
+        uint8_t* sB = base + S::kA;
+        float* sAd = reinterpret_cast<float*>(base + S::kA + S::kB);
+        int32_t* sAs = reinterpret_cast<int32_t*>(base + S::kA + S::kB + S::kAd);
+        uint16_t* sBd = reinterpret_cast<uint16_t*>(base + S::kA + S::kB + S::kAd + S::kAs);
+        const int nkbs = min(kKB, nkb - kb0);
+        // A quants
+        for (int ch = tid; ch < kBM * (S::kAKB / 16); ch += kThreads) {
+            const int r = ch / (S::kAKB / 16), cc = ch % (S::kAKB / 16);
+            const bool ok = r < mrows && cc * 16 < nkbs * 32;
+            const int64_t row = a_row_ptr(r);
+            cp_async16(sA + r * S::kARow + cc * 16, p.aq + row * p.K + (int64_t)kb0 * 32 + (ok ? cc * 16 : 0), ok);
+        }
+        // B quants
+        for (int ch = tid; ch < kBN * (S::kBKB / 16); ch += kThreads) {
+            const int n = ch / (S::kBKB / 16), cc = ch % (S::kBKB / 16);
+            const bool ok = cc * 16 < nkbs * (Q4 ? 16 : 32);
+            cp_async16(sB + n * S::kBRow + cc * 16, b_row_addr(n) + (int64_t)kb0 * (Q4 ? 16 : 32) + (ok ? cc * 16 : 0),
+                       ok);
+        }
+        // scales (plain loads: small)
+        for (int i = tid; i < kBM * kKB; i += kThreads) {
+            const int r = i / kKB, kb = i % kKB;
+            const bool ok = r < mrows && kb < nkbs;
+            const int64_t row = a_row_ptr(r);
+            sAd[i] = ok ? p.ad[row * nkb + kb0 + kb] : 0.f;
+            if (Q4) sAs[i] = ok ? p.as[row * nkb + kb0 + kb] : 0;
+        }
+        for (int i = tid; i < kBN * kKB; i += kThreads) {
+            const int n = i / kKB, kb = i % kKB;
+            sBd[i] = kb < nkbs ? b_scale_addr(n)[kb0 + kb] : (uint16_t)0;
+        }
+    };
+
+    float acc[2][4][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[i][j][q] = 0.f;
+
+    const int nsteps = (nkb + kKB - 1) / kKB;
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (s < nsteps) load_stage(s, s * kKB);
+        cp_async_commit();
+    }
+    const bool sbf = p.scale_bf16 != 0;
+    for (int step = 0; step < nsteps; ++step) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();
+        {   // prefetch step + kStages - 1
+            const int nxt = step + kStages - 1;
+            if (nxt < nsteps) load_stage(nxt % kStages, nxt * kKB);
+            cp_async_commit();
+        }
+        const uint8_t* base = smem + (size_t)(step % kStages) * S::kBytes;
+        const int8_t* sA = reinterpret_cast<const int8_t*>(base);
+        const uint8_t* sB = base + S::kA;
+        const float* sAd = reinterpret_cast<const float*>(base + S::kA + S::kB);
+        const int32_t* sAs = reinterpret_cast<const int32_t*>(base + S::kA + S::kB + S::kAd);
+        const uint16_t* sBd = reinterpret_cast<const uint16_t*>(base + S::kA + S::kB + S::kAd + S::kAs);
+        const int nkbs = min(kKB, nkb - step * kKB);
+        for (int kb = 0; kb < nkbs; ++kb) {
+            uint32_t af[2][4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int r = wm * 32 + i * 16 + g;
+                const uint32_t* ra = reinterpret_cast<const uint32_t*>(sA + r * S::kARow + kb * 32);
+                const uint32_t* rb = reinterpret_cast<const uint32_t*>(sA + (r + 8) * S::kARow + kb * 32);
+                af[i][0] = ra[c];
+                af[i][1] = rb[c];
+                af[i][2] = ra[4 + c];
+                af[i][3] = rb[4 + c];
+            }
+            uint32_t bf[4][2];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = wn * 32 + j * 8 + g;
+                const uint32_t* wr = reinterpret_cast<const uint32_t*>(sB + n * S::kBRow + kb * (Q4 ? 16 : 32));
+                if (Q4) {
+                    const uint32_t w0 = wr[c >> 1], w1 = wr[2 + (c >> 1)];
+                    bf[j][0] = (c & 1) ? (w0 >> 4) & 0x0f0f0f0fu : w0 & 0x0f0f0f0fu;
+                    bf[j][1] = (c & 1) ? (w1 >> 4) & 0x0f0f0f0fu : w1 & 0x0f0f0f0fu;
+                } else {
+                    bf[j][0] = wr[c];
+                    bf[j][1] = wr[4 + c];
+                }
+            }
+            // activation scales (rows g, g+8 of each m16) and weight scales (cols 2c, 2c+1 of each n8)
+            float da[2][2];
+            int sa[2][2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int r = wm * 32 + i * 16 + g + h * 8;
+                    da[i][h] = sAd[r * kKB + kb];
+                    sa[i][h] = Q4 ? sAs[r * kKB + kb] : 0;
+                }
+            float dw[4][2];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) dw[j][h] = scale_to_f32(sBd[(wn * 32 + j * 8 + 2 * c + h) * kKB + kb], sbf);
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    int d[4];
+                    mma_s8<Q4>(d, af[i], bf[j]);
+                    // d0,d1: row g, cols 2c,2c+1; d2,d3: row g+8
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int h = q >> 1, cl = q & 1;
+                        const int is = d[q] - (Q4 ? 8 * sa[i][h] : 0);
+                        acc[i][j][q] += ((float)is * dw[j][cl]) * da[i][h];
+                    }
+                }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // ---------------- epilogue ----------------
+    if (GATE_UP) {
+        // columns interleave (gate, up) per unit: col 2u = gate of unit u, 2u+1 = up.
+        // Thread holds cols 2c, 2c+1 of each n8 -> one unit per (j): h = silu(gate)*up.
+        float* hsm = reinterpret_cast<float*>(smem);  // [kBM][kBN/2 + 1] fp32
+        constexpr int HW = kBN / 2 + 1;
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int r = wm * 32 + i * 16 + g + h * 8;
+                    const int u = (wn * 32 + j * 8 + 2 * c) >> 1;
+                    hsm[r * HW + u] = silu_mul(acc[i][j][2 * h], acc[i][j][2 * h + 1]);
+                }
+        __syncthreads();
+        // requantise per (row, 32-unit block): thread per block
+        const int I = p.N / 2, nbI = I / 32;
+        const int u0 = n0 / 2;
+        for (int t = tid; t < kBM * (kBN / 64); t += kThreads) {
+            const int r = t / (kBN / 64), blk = t % (kBN / 64);
+            if (r >= mrows) continue;
+            float v[32];
+            float amax = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                v[k] = hsm[r * HW + blk * 32 + k];
+                amax = fmaxf(amax, fabsf(v[k]));
+            }
+            const float dd = q8_scale(amax);
+            const float id = q8_inv(dd);
+            int qv[32];
+            int sum = 0;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                qv[k] = q8_quant(v[k], id);
+                sum += qv[k];
+            }
+            uint32_t wv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                uint32_t w = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int el = Q4 ? 8 * (k >> 1) + (k & 1) + 2 * q : 4 * k + q;
+                    w |= (uint32_t)(qv[el] & 0xff) << (8 * q);
+                }
+                wv[k] = w;
+            }
+            const int pos = pos0 + r;
+            const int b = u0 / 32 + blk;
+            uint4* dst = reinterpret_cast<uint4*>(p.hq + (int64_t)pos * I + b * 32);
+            dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            p.hd[(int64_t)pos * nbI + b] = dd;
+            if (Q4) p.hs[(int64_t)pos * nbI + b] = sum;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = wm * 32 + i * 16 + g + h * 8;
+                if (r >= mrows) continue;
+                float* orow = p.out + (int64_t)(pos0 + r) * p.N + n0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col = wn * 32 + j * 8 + 2 * c;
+                    *reinterpret_cast<float2*>(orow + col) = make_float2(acc[i][j][2 * h], acc[i][j][2 * h + 1]);
+                }
+            }
+    }
+}
+
+// y[t][n] = sum_k w[t,k] * out[smap[t,k]][n] in k order, cast.
+__global__ void combine_kernel(const float* out, const int32_t* smap, const float* tw, int T, int K, int H,
+                               void* y, int out_kind) {
+    const int64_t total = (int64_t)T * (H / 4);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / (H / 4)), n4 = (int)(i % (H / 4)) * 4;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const int pos = smap[t * K + k];
+            if (pos < 0) continue;
+            const float w = tw[t * K + k];
+            const float4 v = *reinterpret_cast<const float4*>(out + (int64_t)pos * H + n4);
+            a0 += w * v.x;
+            a1 += w * v.y;
+            a2 += w * v.z;
+            a3 += w * v.w;
+        }
+        const int64_t o = (int64_t)t * H + n4;
+        if (out_kind == 2) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + o) = make_float4(a0, a1, a2, a3);
+        } else if (out_kind == 1) {
+            __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y) + o;
+            yb[0] = __float2bfloat16_rn(a0); yb[1] = __float2bfloat16_rn(a1);
+            yb[2] = __float2bfloat16_rn(a2); yb[3] = __float2bfloat16_rn(a3);
+        } else {
+            __half* yh = reinterpret_cast<__half*>(y) + o;
+            yh[0] = __float2half_rn(a0); yh[1] = __float2half_rn(a1);
+            yh[2] = __float2half_rn(a2); yh[3] = __float2half_rn(a3);
+        }
+    }
+}
+
+}  // namespace gemm
+}  // namespace moe

@@ -220,3 +220,28 @@ def test_quantize_rows_bit_exact(dtype):
     rq, rd = O.quantize_rows_q8_0(xf)
     assert np.array_equal(qs.cpu().numpy(), rq)
     assert np.array_equal(d.cpu().numpy().view(np.uint32), rd.view(np.uint32))
+
+
+@pytest.mark.parametrize("qt,E,H,I,T,K", [
+    (1, 16, 512, 256, 33, 8),
+    (0, 16, 512, 256, 100, 8),
+    (1, 32, 1024, 384, 300, 10),
+    (0, 64, 2048, 768, 64, 8),
+    (1, 128, 2048, 768, 256, 8),
+])
+def test_grouped_gemm_path_matches_oracle(qt, E, H, I, T, K):
+    """T above the decode threshold takes the grouped int8-MMA GEMM path."""
+    y, y_ref, _ = run_engine(qt, E, H, I, T, K, seed=T + E, bad_ids=True)
+    rel, cos = parity(y, y_ref)
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
+
+
+def test_gemm_and_decode_paths_agree(monkeypatch):
+    E, H, I, T, K = 32, 1024, 384, 40, 8
+    outs = []
+    for thr in ("1000", "0"):  # 1000: decode kernel in token slices; 0: grouped GEMM
+        monkeypatch.setenv("MOE_GEMM_MIN_TOKENS", thr)
+        y, y_ref, _ = run_engine(1, E, H, I, T, K, seed=4)
+        outs.append(y)
+    rel, cos = parity(outs[0], outs[1])
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
