@@ -477,7 +477,9 @@ def sweep(handles, dev, args):
             ids, w = torch.ops.nanovllm.moe_route(torch.randn((T, E), generator=g, device=dev), K, True)
             ids_l.append(ids); w_l.append(w); nb.append(int(torch.unique(ids).numel()) * Q4_BYTES_PER_EXPERT)
         n = 200 if T <= 32 else (40 if T <= 1024 else 10)
-        for i in range(3):
+        for h in handles:
+            h.reserve(T, K)  # workspaces sized before timing (no allocation in the timed loop)
+        for i in range(len(handles)):
             torch.ops.nanovllm.moe_forward(xs[i % nrot], ids_l[i % nrot], w_l[i % nrot], handles[i % len(handles)])
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)

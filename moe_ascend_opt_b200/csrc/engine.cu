@@ -477,11 +477,11 @@ int launch_decode(const DecodePlan& pl, cudaStream_t st) {
 
 // ------------------------------------------------------------------ grouped-GEMM path
 // Large token counts: parallel routing, Q8_0 token rows, two grouped GEMMs on the
-// int8 tensor cores, combine.  Only Q8_0 / Q4_0 with 2I and H multiples of 128.
+// int8 tensor cores, combine.  Only Q8_0 / Q4_0 with H and I multiples of 128.
 bool gemm_path_ok(const moe_engine* eng) {
     const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
-    return eng->cfg.quant_type != MOE_AWQ && (2 * I) % gemm::kBN == 0 && H % gemm::kBN == 0 &&
-           eng->cfg.num_experts <= 1024;
+    return eng->cfg.quant_type != MOE_AWQ && (2 * I) % gemm::kBN == 0 && H % gemm::kBN == 0 && I % 128 == 0 &&
+           H % 128 == 0 && eng->cfg.num_experts <= 1024;
 }
 
 struct GemmWs {
@@ -778,7 +778,11 @@ extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t t
     if (int rc = check_engine(eng)) return rc;
     if (max_tokens < 0 || top_k <= 0) return fail(MOE_ERR_INVALID, "bad reserve size");
     DeviceGuard g(eng->cfg.device);
-    return ensure_workspace(eng, max_tokens * top_k);
+    if (max_tokens > eng->gemm_min_tokens && gemm_path_ok(eng)) {  // the grouped-GEMM path's workspace
+        GemmWs w;
+        if (int rc = gemm_workspace(eng, max_tokens, top_k, w)) return rc;
+    }
+    return ensure_workspace(eng, std::min<int64_t>(max_tokens, 64) * top_k);
 }
 
 extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const int32_t* topk_ids,

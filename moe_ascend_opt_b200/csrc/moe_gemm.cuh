@@ -258,29 +258,30 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
     const int pos0 = p.starts[e] + m0;
     const int mrows = min(kBM, cnt - m0);
     const int n0 = nt * kBN;
-    const int nkb = p.K / 32;
+    const int nkb = p.K / 32;  // multiple of kKB (K % 128 == 0)
 
-    // per-row source pointers (loader threads)
-    // A: 64 rows x (kKB*32) bytes per stage = 64 x 8 chunks of 16 B -> 2 chunks per thread
-    // B: 128 rows x kBKB bytes -> (Q4: 4 chunks, Q8: 8 chunks per row)
-    auto a_row_ptr = [&](int r) -> int64_t {  // element offset of row r (clamped)
-        const int rr = min(r, mrows - 1);
+    // source rows of the tile's activations, resolved once (gathered through tokmap for gate_up)
+    __shared__ int64_t s_arow[kBM];
+    for (int r = tid; r < kBM; r += kThreads) {
+        const int rr = min(r, max(mrows, 1) - 1);
         const int pos = pos0 + rr;
-        const int64_t row = GATE_UP ? (int64_t)(p.tokmap[pos] / p.topk) : (int64_t)pos;
-        return row;
-    };
+        s_arow[r] = GATE_UP ? (int64_t)(p.tokmap[pos] / p.topk) : (int64_t)pos;
+    }
+    __syncthreads();
+    const uint8_t* wexp = p.wbase + (int64_t)e * p.nrec * p.rec;
     auto b_row_addr = [&](int n) -> const uint8_t* {
         const int gn = n0 + n;
-        const int rec = gn / p.rows_per_rec, sub = gn % p.rows_per_rec;
-        return p.wbase + ((int64_t)e * p.nrec + rec) * p.rec + (int64_t)sub * p.rs;
+        const int rec = gn / p.rows_per_rec, sub = gn - rec * p.rows_per_rec;
+        return wexp + (int64_t)rec * p.rec + (int64_t)sub * p.rs;
     };
-    auto b_scale_addr = [&](int n) -> const uint16_t* {
+    auto b_scale_addr = [&](int n) -> const uint8_t* {
         const int gn = n0 + n;
-        const int rec = gn / p.rows_per_rec, sub = gn % p.rows_per_rec;
-        return reinterpret_cast<const uint16_t*>(p.wbase + ((int64_t)e * p.nrec + rec) * p.rec + p.sc_off +
-                                                 (int64_t)sub * p.ss);
+        const int rec = gn / p.rows_per_rec, sub = gn - rec * p.rows_per_rec;
+        return wexp + (int64_t)rec * p.rec + p.sc_off + (int64_t)sub * p.ss;
     };
 
+    // every stage is loaded with cp.async only (quants 16 B, activation scales / sums
+    // 16 B = 4 blocks, weight scales 8 B = 4 blocks); K is a multiple of 128.
     auto load_stage = [&](int st, int kb0) {
         uint8_t* base = smem + (size_t)st * S::kBytes;
         int8_t* sA = reinterpret_cast<int8_t*>(base);
@@ -288,32 +289,21 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         float* sAd = reinterpret_cast<float*>(base + S::kA + S::kB);
         int32_t* sAs = reinterpret_cast<int32_t*>(base + S::kA + S::kB + S::kAd);
         uint16_t* sBd = reinterpret_cast<uint16_t*>(base + S::kA + S::kB + S::kAd + S::kAs);
-        const int nkbs = min(kKB, nkb - kb0);
-        // A quants
         for (int ch = tid; ch < kBM * (S::kAKB / 16); ch += kThreads) {
             const int r = ch / (S::kAKB / 16), cc = ch % (S::kAKB / 16);
-            const bool ok = r < mrows && cc * 16 < nkbs * 32;
-            const int64_t row = a_row_ptr(r);
-            cp_async16(sA + r * S::kARow + cc * 16, p.aq + row * p.K + (int64_t)kb0 * 32 + (ok ? cc * 16 : 0), ok);
+            cp_async16(sA + r * S::kARow + cc * 16, p.aq + s_arow[r] * p.K + (int64_t)kb0 * 32 + cc * 16, r < mrows);
         }
-        // B quants
         for (int ch = tid; ch < kBN * (S::kBKB / 16); ch += kThreads) {
             const int n = ch / (S::kBKB / 16), cc = ch % (S::kBKB / 16);
-            const bool ok = cc * 16 < nkbs * (Q4 ? 16 : 32);
-            cp_async16(sB + n * S::kBRow + cc * 16, b_row_addr(n) + (int64_t)kb0 * (Q4 ? 16 : 32) + (ok ? cc * 16 : 0),
-                       ok);
+            cp_async16(sB + n * S::kBRow + cc * 16, b_row_addr(n) + (int64_t)kb0 * (Q4 ? 16 : 32) + cc * 16, true);
         }
-        // scales (plain loads: small)
-        for (int i = tid; i < kBM * kKB; i += kThreads) {
-            const int r = i / kKB, kb = i % kKB;
-            const bool ok = r < mrows && kb < nkbs;
-            const int64_t row = a_row_ptr(r);
-            sAd[i] = ok ? p.ad[row * nkb + kb0 + kb] : 0.f;
-            if (Q4) sAs[i] = ok ? p.as[row * nkb + kb0 + kb] : 0;
+        for (int r = tid; r < kBM; r += kThreads) {
+            cp_async16(sAd + r * kKB, p.ad + s_arow[r] * nkb + kb0, r < mrows);
+            if (Q4) cp_async16(sAs + r * kKB, p.as + s_arow[r] * nkb + kb0, r < mrows);
         }
-        for (int i = tid; i < kBN * kKB; i += kThreads) {
-            const int n = i / kKB, kb = i % kKB;
-            sBd[i] = kb < nkbs ? b_scale_addr(n)[kb0 + kb] : (uint16_t)0;
+        for (int n = tid; n < kBN; n += kThreads) {
+            const uint32_t d = smem_u32(sBd + n * kKB);
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(b_scale_addr(n) + kb0 * 2) : "memory");
         }
     };
 
@@ -345,8 +335,8 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         const float* sAd = reinterpret_cast<const float*>(base + S::kA + S::kB);
         const int32_t* sAs = reinterpret_cast<const int32_t*>(base + S::kA + S::kB + S::kAd);
         const uint16_t* sBd = reinterpret_cast<const uint16_t*>(base + S::kA + S::kB + S::kAd + S::kAs);
-        const int nkbs = min(kKB, nkb - step * kKB);
-        for (int kb = 0; kb < nkbs; ++kb) {
+#pragma unroll 2
+        for (int kb = 0; kb < kKB; ++kb) {
             uint32_t af[2][4];
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
