@@ -39,8 +39,8 @@ Q8_BYTES_PER_EXPERT = (2 * I * H) + (2 * I * (H // 32) * 2) + (H * I) + (H * (I 
 METRIC = "fused MoE layer µs & effective weight GB/s vs HBM peak, tokens 1–4096, 1/2/4/8 GPU"
 HBM_FALLBACK = 6650.0
 # DRAM bytes (read + write) per launch of moe_decode_kernel<Q4> at this workload, from the
-# ncu capture summarised in profiles/moe_decode_q4_T1.md (None until captured).
-NCU_TRAFFIC_BYTES = None
+# ncu capture summarised in profiles/moe_decode_q4_T1.md.
+NCU_TRAFFIC_BYTES = 21320960
 
 
 def peaks():
