@@ -110,7 +110,7 @@ MOE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
-// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
+// 1-D bulk copy global -> shared, completion counted on `bar` (plain, one destination CTA).
 // dst, src and bytes must be multiples of 16.
 MOE_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
