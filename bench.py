@@ -305,7 +305,7 @@ def run_ours(args):
     graphs = None
     cycle_graph = None
     ncycle = int(np.lcm(nsets, nin))
-    if world == 1 and not args.no_graph:
+    if world == 1 and not args.no_graph:  # N>1: eager launches + NCCL (its capture is not used)
         try:
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
@@ -399,7 +399,7 @@ def run_ours(args):
                       "avg_active_experts": round(avg_bytes / Q4_BYTES_PER_EXPERT, 2)},
            "gpu_launches": args.steps * (1 if world == 1 else 1),
            "clocks": clocks}
-    if world == 1:
+    if True:
         out["roofline"] = {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
                            "frac": round(value / peak, 4), "peak_source": peak_kind,
                            "traffic": NCU_TRAFFIC_BYTES,
