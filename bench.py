@@ -91,6 +91,88 @@ def make_q4_layer(seed, device, e_lo=0, e_hi=E):
     return gu_qs, gu_d, dn_qs, dn_d
 
 
+SHAPES = {"qwen": (2048, 768, 128), "minimax": (3072, 1536, 256)}  # H, I, E (top-8 both)
+
+
+def bytes_per_expert(quant, H_, I_, G=128):
+    """Algorithmic weight bytes of one expert (gate_up + down, quants + scales (+ zeros))."""
+    if quant == "q4":
+        return (2 * I_ * H_ // 2) + (2 * I_ * (H_ // 32) * 2) + (H_ * I_ // 2) + (H_ * (I_ // 32) * 2)
+    if quant == "q8":
+        return (2 * I_ * H_) + (2 * I_ * (H_ // 32) * 2) + (H_ * I_) + (H_ * (I_ // 32) * 2)
+    # AWQ: int4 weights, bf16 scales and int4 zeros per group of G along K
+    return (2 * I_ * H_ // 2) + (2 * I_ * (H_ // G) * 2) + (2 * I_ * (H_ // G) // 2) + \
+           (H_ * I_ // 2) + (H_ * (I_ // G) * 2) + (H_ * (I_ // G) // 2)
+
+
+def q8_quantize_torch(w):
+    """fp32 [..., N, Kd] -> (int8 [..., N, Kd], fp16 [..., N, Kd/32]): d = amax/127, RNE."""
+    import torch
+    shp = w.shape
+    b = w.reshape(*shp[:-1], shp[-1] // 32, 32)
+    d32 = b.abs().amax(-1) / 127.0
+    idv = torch.where(d32 != 0, 1.0 / d32, torch.zeros_like(d32))
+    q = torch.clamp(torch.round(b * idv.unsqueeze(-1)), -128, 127).to(torch.int8)
+    return q.reshape(shp), d32.to(torch.float16)
+
+
+def make_layer(quant, shape, seed, device, e_lo, e_hi, world, rank):
+    """A loaded MoEInfer handle with one synthetic layer (BASELINE configs value distributions)."""
+    import torch
+    H_, I_, E_ = SHAPES[shape]
+    qt = {"q8": 0, "q4": 1, "awq": 2}[quant]
+    h = torch.classes.nanovllm.MoEInfer(E_, H_, I_, qt)
+    if quant == "awq":
+        h.set_group_size(128)
+    if world > 1:
+        h.set_expert_parallel(rank, world)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    if quant == "awq":  # q, z uniform [0,15] (random words), bf16 scales U(0.001, 0.01)
+        G = 128
+        def words(*shp):
+            return torch.randint(-2 ** 31, 2 ** 31 - 1, shp, generator=g, device=device, dtype=torch.int64).to(torch.int32)
+        def scales(*shp):
+            return (torch.rand(shp, generator=g, device=device) * 0.009 + 0.001).to(torch.bfloat16)
+        h.store_awq(words(E_, H_, 2 * I_ // 8), scales(E_, H_ // G, 2 * I_), words(E_, H_ // G, 2 * I_ // 8),
+                    words(E_, I_, H_ // 8), scales(E_, I_ // G, H_), words(E_, I_ // G, H_ // 8))
+        return h
+    qfn = q4_quantize_torch if quant == "q4" else q8_quantize_torch
+    kq = 8 if quant == "q4" else 1
+    qdt = torch.int32 if quant == "q4" else torch.int8
+    gu_qs = torch.zeros((E_, 2 * I_, H_ // kq), dtype=qdt, device=device)
+    gu_d = torch.zeros((E_, 2 * I_, H_ // 32), dtype=torch.float16, device=device)
+    dn_qs = torch.zeros((E_, H_, I_ // kq), dtype=qdt, device=device)
+    dn_d = torch.zeros((E_, H_, I_ // 32), dtype=torch.float16, device=device)
+    step = 8
+    for e0 in range(0, E_, step):
+        e1 = min(E_, e0 + step)
+        wg = torch.randn((e1 - e0, 2 * I_, H_), generator=g, device=device) * 0.02
+        wd = torch.randn((e1 - e0, H_, I_), generator=g, device=device) * 0.02
+        if e1 <= e_lo or e0 >= e_hi:
+            continue
+        gu_qs[e0:e1], gu_d[e0:e1] = qfn(wg)
+        dn_qs[e0:e1], dn_d[e0:e1] = qfn(wd)
+        del wg, wd
+    h.store_quantized_repack(gu_qs, gu_d, dn_qs, dn_d)
+    return h
+
+
+def make_routing(kind, T, E_, K_, g, device):
+    """softmax: top-K of N(0,1) logits with renormalised softmax weights (the engine's router);
+    zipf: K distinct experts per token drawn with p(rank r) ~ r^-1.2 over a fixed random expert
+    order, weights 1/K (BASELINE configs[2] run B)."""
+    import torch
+    if kind == "softmax":
+        return torch.ops.nanovllm.moe_route(torch.randn((T, E_), generator=g, device=device), K_, True)
+    perm = torch.randperm(E_, generator=g, device=device)
+    p = (torch.arange(1, E_ + 1, device=device, dtype=torch.float32) ** -1.2)
+    ranks = torch.multinomial(p.expand(T, E_), K_, replacement=False, generator=g)
+    ids = perm[ranks].to(torch.int32).contiguous()
+    w = torch.full((T, K_), 1.0 / K_, device=device, dtype=torch.float32)
+    return ids, w
+
+
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
     def __init__(self, out_path, gpu_index=0):
@@ -263,31 +345,27 @@ def run_ours(args):
 
     T = args.tokens
     nsets = args.sets
+    H, I, E = SHAPES[args.shape]
+    bpe = bytes_per_expert(args.quant, H, I)
     el = E // world
     e_lo, e_hi = rank * el, (rank + 1) * el
     handles = []
     for s in range(nsets):
-        h = torch.classes.nanovllm.MoEInfer(E, H, I, 1)
-        if world > 1:
-            h.set_expert_parallel(rank, world)
-        ws = make_q4_layer(1000 + s, dev, e_lo, e_hi)
-        h.store_quantized_repack(*ws)
-        del ws
+        h = make_layer(args.quant, args.shape, 1000 + s, dev, e_lo, e_hi, world, rank)
         h.reserve(max(T, 32), K)
         handles.append(h)
     torch.cuda.synchronize()
 
-    # per-step inputs: hidden + routing through the engine's router
+    # per-step inputs: hidden + routing
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     nin = max(nsets, 16)
     xs, idss, wss, nbytes = [], [], [], []
     for i in range(nin):
         x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
-        logits = torch.randn((T, E), generator=g, device=dev)
-        ids, w = torch.ops.nanovllm.moe_route(logits, K, True)
+        ids, w = make_routing(args.routing, T, E, K, g, dev)
         xs.append(x); idss.append(ids); wss.append(w)
-        nbytes.append(int(torch.unique(ids).numel()) * Q4_BYTES_PER_EXPERT)
+        nbytes.append(int(torch.unique(ids).numel()) * bpe)
     combine_out = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(nin)]
 
     def step(i):
@@ -381,6 +459,8 @@ def run_ours(args):
     clocks = clk.summary()
 
     avg_bytes = sum(nbytes[i % nin] for i in range(args.steps)) / args.steps
+    qname = {"q4": "Q4_0", "q8": "Q8_0", "awq": "AWQ W4A16 g128"}[args.quant]
+    default_wl = args.quant == "q4" and args.shape == "qwen" and args.routing == "softmax"
     ms_step = total_ms / args.steps
     value = avg_bytes / (ms_step * 1e-3) / 1e9
     peak, peak_kind = peaks()
@@ -389,14 +469,15 @@ def run_ours(args):
            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "us_per_layer": round(ms_step * 1e3, 3),
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
            "data": "synthetic",
-           "config": {"workload": f"Q4_0 fused MoE layer H{H} I{I} E{E} top{K} T={T} (BASELINE configs[1])",
+           "config": {"workload": f"{qname} fused MoE layer H{H} I{I} E{E} top{K} T={T}"
+                                  + (" (BASELINE configs[1])" if default_wl else f", {args.routing} routing"),
                       "tokens": T, "weight_sets": nsets,
                       "l2": f"inputs larger than L2: {nsets} rotating weight sets x {E} experts "
-                            f"({nsets * E * Q4_BYTES_PER_EXPERT / 1e9:.1f} GB) and {nin} rotating routings",
+                            f"({nsets * E * bpe / 1e9:.1f} GB) and {nin} rotating routings",
                       "parallelism": f"ep{world}" if world > 1 else "single",
                       "launch": (f"cuda_graph ({ncycle} layer steps per graph replay)" if cycle_graph is not None
                                  else "eager"),
-                      "avg_active_experts": round(avg_bytes / Q4_BYTES_PER_EXPERT, 2)},
+                      "avg_active_experts": round(avg_bytes / bpe, 2)},
            "gpu_launches": args.steps * (1 if world == 1 else 1),
            "clocks": clocks}
     if True:
@@ -404,7 +485,7 @@ def run_ours(args):
                            "frac": round(value / peak, 4), "peak_source": peak_kind,
                            "traffic": NCU_TRAFFIC_BYTES,
                            "algorithmic_bytes_per_launch": round(avg_bytes),
-                           "kernel": "moe_decode_kernel<Q4_0>"}
+                           "kernel": "moe_decode_kernel" if T <= 32 or args.quant == "awq" else "grouped_gemm_kernel"}
     # end-to-end through the public op with host buffers and copies in the timed region
     if rank == 0 or world > 1:
         xh = [x.cpu().pin_memory() for x in xs]
@@ -450,10 +531,10 @@ def run_ours(args):
                       "ms_per_step": round(ems / n_e2e, 6), "steps": n_e2e,
                       "h2d_bytes_per_step": T * H * 2 + T * K * 8, "d2h_bytes_per_step": T * H * 2,
                       "api": "torch.ops.nanovllm.moe_forward (eager, pinned host buffers)"}
-    if world == 1 and not args.no_cpu:
+    if world == 1 and not args.no_cpu and default_wl:
         out["cpu_baseline"] = cpu_baseline(T)
     if args.sweep and world == 1:
-        out["sweep"] = sweep(handles, dev, args)
+        out["sweep"] = sweep(handles, dev, args, H, I, E, bpe)
     if rank == 0:
         print(json.dumps(out))
         sys.stdout.flush()
@@ -463,19 +544,19 @@ def run_ours(args):
     return 0
 
 
-def sweep(handles, dev, args):
+def sweep(handles, dev, args, H, I, E, bpe):
     """Eager per-T timing (events) for the token sweep of BASELINE configs[1]."""
     import torch
     res = {}
     g = torch.Generator(device=dev)
     g.manual_seed(11)
-    for T in (1, 4, 8, 32, 128, 1024, 4096):
+    for T in [int(v) for v in args.sweep_tokens.split(",")]:
         nrot = 16 if T <= 32 else 4
         xs, ids_l, w_l, nb = [], [], [], []
         for i in range(nrot):
             xs.append(torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16))
-            ids, w = torch.ops.nanovllm.moe_route(torch.randn((T, E), generator=g, device=dev), K, True)
-            ids_l.append(ids); w_l.append(w); nb.append(int(torch.unique(ids).numel()) * Q4_BYTES_PER_EXPERT)
+            ids, w = make_routing(args.routing, T, E, K, g, dev)
+            ids_l.append(ids); w_l.append(w); nb.append(int(torch.unique(ids).numel()) * bpe)
         n = 200 if T <= 32 else (40 if T <= 1024 else 10)
         for h in handles:
             h.reserve(T, K)  # workspaces sized before timing (no allocation in the timed loop)
@@ -493,7 +574,7 @@ def sweep(handles, dev, args):
         b = sum(nb[i % nrot] for i in range(n)) / n
         res[f"T{T}"] = {"us": round(ms * 1e3, 2), "GB/s": round(b / (ms * 1e-3) / 1e9, 1),
                         "TFLOP/s": round(6.0 * T * K * H * I / (ms * 1e-3) / 1e12, 2),
-                        "active_experts": round(b / Q4_BYTES_PER_EXPERT, 1)}
+                        "active_experts": round(b / bpe, 1)}
     return res
 
 
@@ -508,6 +589,10 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--quant", default="q4", choices=["q4", "q8", "awq"])
+    ap.add_argument("--shape", default="qwen", choices=["qwen", "minimax"])
+    ap.add_argument("--routing", default="softmax", choices=["softmax", "zipf"])
+    ap.add_argument("--sweep-tokens", default="1,4,8,32,128,1024,4096")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock soak (profiling runs)")
     ap.add_argument("--cpu-worker", type=float, default=None)
     args = ap.parse_args()

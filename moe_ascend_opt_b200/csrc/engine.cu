@@ -402,13 +402,13 @@ struct DecodePlan {
     int grid;
 };
 
-bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
+bool plan_decode_lpr(const moe_engine* eng, int T, int K, int lpr0, DecodePlan& pl) {
     const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
     const int TK = T * K, nb1 = H / 32, nb2 = I / 32;
     const int G = eng->num_sms;
     DecodeParams& p = pl.p;
     std::memset(&p, 0, sizeof(p));
-    int lpr = 4;  // phase 2: 4 lanes per down row, 8 rows per item
+    int lpr = lpr0;  // phase 2: lanes per down row (32 / lpr rows per item)
     while (lpr > 1 && nb2 % lpr != 0) lpr >>= 1;
     p.lanes_per_row = lpr;
     const int rpg = 32 / lpr;
@@ -447,6 +447,14 @@ bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
     pl.smem = (size_t)off;
     pl.grid = G;
     return true;
+}
+
+// Prefer 4 lanes per down row (8-row items); wider rows (large I) take more lanes per row so
+// that two ring slots per warp still fit in shared memory.
+bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
+    for (int lpr : {4, 8, 16, 32})
+        if (plan_decode_lpr(eng, T, K, lpr, pl)) return true;
+    return false;
 }
 
 template <int FMT>
