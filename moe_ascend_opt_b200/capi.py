@@ -138,7 +138,7 @@ class Engine:
         call("moe_engine_export_expert", self.h, e, which, qs_out.ctypes.data, d_out.ctypes.data)
 
     def timeline(self, enable=None):
-        """Enable/disable per-CTA phase stamps, or (enable=None) fetch the last launch's [CTAs, 16] ns stamps."""
+        """Enable/disable per-CTA phase stamps, or (enable=None) fetch the last launch's [CTAs, 20] stamps."""
         import numpy as np
         n = C.c_int32()
         if enable is not None:
@@ -147,7 +147,7 @@ class Engine:
         call("moe_engine_debug_timeline", self.h, 1, None, 0, C.byref(n))
         out = np.zeros(n.value, np.uint64)
         call("moe_engine_debug_timeline", self.h, 1, out.ctypes.data, n.value, C.byref(n))
-        return out.reshape(-1, 16)
+        return out.reshape(-1, 20)
 
     def close(self):
         if self.h:

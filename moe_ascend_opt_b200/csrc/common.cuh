@@ -120,6 +120,22 @@ MOE_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
         : "memory");
 }
 
+// Same copy with an L2 cache-policy operand (e.g. evict-first for data read once).
+MOE_DEV void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 policy: lines filled by the accesses that carry it are the first to be evicted.
+MOE_DEV uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 MOE_DEV void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -145,14 +161,20 @@ MOE_DEV unsigned long long atom_add_release_gpu_u64(unsigned long long* p, unsig
 // Grid barrier over `nblocks` co-resident CTAs (cooperative launch), one thread
 // per CTA.  `ctr` counts arrivals monotonically over all launches; launch n
 // (0-based, read by barrier_launch_index at its start) is released once the
-// counter reaches (n+1)*nblocks.  The arrival is a fire-and-forget release
-// reduction (orders this CTA's earlier global writes before it), then acquire
+// counter reaches (n+1)*nblocks.  The arrival is a gpu-scope fence (orders this
+// CTA's earlier global writes before it) and a fire-and-forget reduction, then acquire
 // polling.  Returns false (and sets *err) when the wait budget ran out.
-MOE_DEV bool grid_barrier(unsigned long long* ctr, uint32_t nblocks, unsigned long long target, int32_t* err) {
+MOE_DEV bool grid_barrier(unsigned long long* ctr, uint32_t nblocks, unsigned long long target, int32_t* err,
+                          unsigned long long* stamps = nullptr) {
     (void)nblocks;
-    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(ctr), "l"(1ull) : "memory");
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    if (stamps) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(stamps[0]));
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(ctr), "l"(1ull) : "memory");
     for (uint32_t it = 0; it < kSpinLimit; ++it) {
-        if (ld_acquire_gpu_u64(ctr) >= target) return true;
+        if (ld_acquire_gpu_u64(ctr) >= target) {
+            if (stamps) asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(stamps[1]));
+            return true;
+        }
         if (it > 4096) __nanosleep(256);  // hot spin first: the barrier is on the critical path
     }
     atomicExch(reinterpret_cast<int*>(err), kErrGridBarrier);

@@ -13,7 +13,7 @@
 
 #include "../../include/moe_b200.h"
 #include "common.cuh"
-#include "moe_decode.cuh"
+#include "moe_decode_sk.cuh"
 #include "moe_gemm.cuh"
 
 using namespace moe;
@@ -53,15 +53,23 @@ struct moe_engine {
     // AWQ: per-row scale field = [bf16 scales x ngroups][u8 zeros x ngroups], padded
     int64_t unit_bytes() const { return 2 * (int64_t)(rs1 + ss1); }
     int64_t row_bytes() const { return (int64_t)(rs2 + ss2); }
+    // down weights re-laid for the split-K decode kernel (Q8_0 / Q4_0): [E][I/32][H/32] slices
+    uint8_t* dk = nullptr;
+    bool use_sk = true;  // decode through moe_decode_sk_kernel when the layout allows
+    int32_t sk_cost_a = 3;  // its chunk cost model: streaming share per chunk vs one token of compute
+    int32_t sk_min_chunks_per_cta = 2;  // use it from this many (unique expert x I/32) chunks per CTA
+    float* part = nullptr;  // per-CTA fp32 partial tiles [num_sms][part_cap][H] of the split-K kernel
+    int64_t part_cap = 0;
     // workspace
     float* h_ws = nullptr;
     int64_t h_cap = 0;  // positions
-    uint32_t* hmax = nullptr;  // [2][h_cap * I/32]
     uint32_t* bar = nullptr;
     int32_t* err = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     bool timed = false;
     int64_t gemm_min_tokens = 32;  // forwards with more tokens take the grouped-GEMM path
+    int32_t decode_flags = kFlagEvictFirst;
+    int32_t dist_min_blocks = -1;  // decode: requantise h before the barrier from this many blocks (-1: 2 x SMs)
     // grouped-GEMM path workspace (one allocation, carved per call)
     uint8_t* gws = nullptr;
     size_t gws_bytes = 0;
@@ -300,6 +308,10 @@ int stage_to_device(const void* src, size_t bytes, int on_device, cudaStream_t s
     return MOE_OK;
 }
 
+int64_t sk_slice_bytes(const moe_engine* eng) {
+    return 32 * (eng->cfg.quant_type == MOE_Q4_0 ? 16 : 32) + 64;
+}
+
 int alloc_q_layout(moe_engine* eng) {
     const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
     const int qt = eng->cfg.quant_type;
@@ -322,7 +334,41 @@ int alloc_q_layout(moe_engine* eng) {
         CUDA_TRY(cudaMalloc(&eng->dn, (size_t)E * H * eng->row_bytes()));
         CUDA_TRY(cudaMemset(eng->gu, 0, (size_t)E * I * eng->unit_bytes()));
         CUDA_TRY(cudaMemset(eng->dn, 0, (size_t)E * H * eng->row_bytes()));
+        if (qt != MOE_AWQ) {
+            const size_t dk_bytes = (size_t)E * (I / 32) * (H / 32) * sk_slice_bytes(eng);
+            CUDA_TRY(cudaMalloc(&eng->dk, dk_bytes));
+            CUDA_TRY(cudaMemset(eng->dk, 0, dk_bytes));
+        }
     }
+    return MOE_OK;
+}
+
+// Row records of down -> split-K chunks: one thread per (expert, chunk jb, slice s, row l).
+__global__ void pack_down_chunks_kernel(uint8_t* dk, const uint8_t* dn, int64_t E, int64_t H, int64_t I, int64_t rec,
+                                        int rs2, int BB, int64_t e0, int64_t e1) {
+    const int64_t nb2 = I / 32, nsl = H / 32;
+    const int64_t n = (e1 - e0) * nb2 * nsl * 32;
+    const int64_t SB = 32 * BB + 64;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int l = (int)(i & 31);
+        const int64_t sl = (i >> 5) % nsl, jb = ((i >> 5) / nsl) % nb2, e = e0 + (i >> 5) / (nsl * nb2);
+        const uint8_t* src = dn + (e * H + sl * 32 + l) * rec;
+        uint8_t* dst = dk + ((e * nb2 + jb) * nsl + sl) * SB;
+        const uint4* q = reinterpret_cast<const uint4*>(src + jb * BB);
+        uint4* d = reinterpret_cast<uint4*>(dst + (size_t)l * BB);
+        d[0] = q[0];
+        if (BB == 32) d[1] = q[1];
+        reinterpret_cast<uint16_t*>(dst + 32 * BB)[l] = reinterpret_cast<const uint16_t*>(src + rs2)[jb];
+    }
+}
+
+int build_down_chunks(moe_engine* eng, int64_t e0, int64_t e1, cudaStream_t st) {
+    if (!eng->dk) return MOE_OK;
+    const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    const int BB = eng->cfg.quant_type == MOE_Q4_0 ? 16 : 32;
+    pack_down_chunks_kernel<<<eng->num_sms * 8, 256, 0, st>>>(eng->dk, eng->dn, eng->cfg.num_experts, H, I,
+                                                               eng->row_bytes(), eng->rs2, BB, e0, e1);
+    CUDA_TRY(cudaGetLastError());
     return MOE_OK;
 }
 
@@ -384,13 +430,8 @@ int ensure_workspace(moe_engine* eng, int64_t positions) {
     while (cap < positions) cap *= 2;
     CUDA_TRY(cudaDeviceSynchronize());  // the old buffers may still be in use by queued work
     if (eng->h_ws) CUDA_TRY(cudaFree(eng->h_ws));
-    if (eng->hmax) CUDA_TRY(cudaFree(eng->hmax));
     eng->h_ws = nullptr;
-    eng->hmax = nullptr;
-    const size_t hm = (size_t)cap * (eng->cfg.intermediate_size / 32);
     CUDA_TRY(cudaMalloc(&eng->h_ws, (size_t)cap * eng->cfg.intermediate_size * sizeof(float)));
-    CUDA_TRY(cudaMalloc(&eng->hmax, 2 * hm * sizeof(uint32_t)));
-    CUDA_TRY(cudaMemset(eng->hmax, 0, 2 * hm * sizeof(uint32_t)));
     eng->h_cap = cap;
     return MOE_OK;
 }
@@ -400,7 +441,75 @@ struct DecodePlan {
     DecodeParams p;
     size_t smem;
     int grid;
+    bool sk = false;  // split-K kernel (moe_decode_sk_kernel) with layout L
+    SkLayout L{};
 };
+
+int ensure_part(moe_engine* eng, int64_t tokens) {
+    if (tokens <= eng->part_cap) return MOE_OK;
+    int64_t cap = eng->part_cap ? eng->part_cap : 8;
+    while (cap < tokens) cap *= 2;
+    CUDA_TRY(cudaDeviceSynchronize());  // the old buffer may still be in use by queued work
+    if (eng->part) CUDA_TRY(cudaFree(eng->part));
+    eng->part = nullptr;
+    CUDA_TRY(cudaMalloc(&eng->part, (size_t)eng->num_sms * cap * eng->cfg.hidden_size * sizeof(float)));
+    eng->part_cap = cap;
+    return MOE_OK;
+}
+
+// Shared-memory plan of the split-K decode kernel for T tokens; false if it does not fit
+// (or the engine cannot use it).
+bool plan_decode_sk(const moe_engine* eng, int T, int K, DecodePlan& pl) {
+    if (!eng->use_sk || !eng->dk || eng->cfg.quant_type == MOE_AWQ) return false;
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    const int TK = T * K, nb1 = H / 32, nb2 = I / 32, nsl = H / 32;
+    const int G = eng->num_sms;
+    // with fewer than ~2 chunks per CTA the chunk granularity leaves CTAs with twice the
+    // work of others (one token: 8 experts x I/32 chunks); the barrier kernel splits
+    // gate_up evenly by rows there
+    if ((int64_t)std::min(E, TK) * nb2 < (int64_t)eng->sk_min_chunks_per_cta * G) return false;
+    DecodeParams& p = pl.p;
+    std::memset(&p, 0, sizeof(p));
+    SkLayout& L = pl.L;
+    int64_t off = (int64_t)(3 * TK + 5 * E + 4) * 4;
+    L.off_tw = (int)off;
+    off = round_up(off + (int64_t)TK * 12 + (int64_t)(E + 1) * 4, 128);
+    L.off_a = (int)off;
+    const int64_t xbytes = (int64_t)T * H + (int64_t)T * nb1 * 8, tile = (int64_t)T * H * 4;
+    off += round_up(std::max({xbytes, tile, (int64_t)kThreads * 4}), 128);  // + the reduction's group sums
+    L.off_h = (int)off;
+    // h slots per CTA: the cost share of one CTA bounds its (chunk, token) pairs
+    const int64_t nbmax = (int64_t)std::min(E, TK) * nb2, A = eng->sk_cost_a;
+    L.hslots = (int)((nbmax * A + (int64_t)TK * nb2 + G - 1) / G + A + 2 * T + 1);  // + float rounding of the split
+    off += round_up((int64_t)L.hslots * 128, 128);
+    L.spw = (nsl + kWarps - 1) / kWarps;
+    const int64_t SB = sk_slice_bytes(eng);
+    const int64_t unit_bytes = eng->unit_bytes(), down_item = L.spw * SB;
+    const int64_t avail = (int64_t)eng->max_smem - off - 1024;
+    const int64_t per_warp = avail / kWarps;
+    int upi = 4;
+    while (upi > 1 && 2 * round_up(std::max((int64_t)upi * unit_bytes, down_item), 128) > per_warp) upi >>= 1;
+    const int64_t slot = round_up(std::max((int64_t)upi * unit_bytes, down_item), 128);
+    const int slots = (int)std::min<int64_t>(6, per_warp / slot);
+    if (slots < 2) return false;
+    p.units_per_item = upi;
+    p.slots = slots;
+    p.slot_bytes = (int)slot;
+    off = round_up(off + 8 * kWarps * slots, 128);
+    p.off_ring = (int)off;
+    off += (int64_t)kWarps * slots * slot;
+    if (off > eng->max_smem - 256) return false;
+    p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
+    p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
+    p.scale_bf16 = eng->scale_bf16;
+    p.group = eng->cfg.group_size;
+    p.flags = eng->decode_flags;
+    p.sk_cost_a = eng->sk_cost_a;
+    pl.smem = (size_t)off;
+    pl.grid = G;
+    pl.sk = true;
+    return true;
+}
 
 bool plan_decode_lpr(const moe_engine* eng, int T, int K, int lpr0, DecodePlan& pl) {
     const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
@@ -444,6 +553,8 @@ bool plan_decode_lpr(const moe_engine* eng, int T, int K, int lpr0, DecodePlan& 
     p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
     p.scale_bf16 = eng->scale_bf16;
     p.group = eng->cfg.group_size;
+    p.flags = eng->decode_flags;
+    p.dist_min_blocks = eng->dist_min_blocks >= 0 ? eng->dist_min_blocks : 2 * G;
     pl.smem = (size_t)off;
     pl.grid = G;
     return true;
@@ -458,7 +569,32 @@ bool plan_decode(const moe_engine* eng, int T, int K, DecodePlan& pl) {
 }
 
 template <int FMT>
+int launch_decode_sk(const DecodePlan& pl, cudaStream_t st) {
+    auto kern = moe_decode_sk_kernel<FMT>;
+    static thread_local int smem_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && smem_set[dev] < (int)pl.smem) {
+        CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem));
+        smem_set[dev] = (int)pl.smem;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // the grid barrier needs every CTA resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, pl.p, pl.L));
+    return MOE_OK;
+}
+
+template <int FMT>
 int launch_decode(const DecodePlan& pl, cudaStream_t st) {
+    if (pl.sk) return FMT == kQ4 ? launch_decode_sk<kQ4>(pl, st) : launch_decode_sk<kQ8>(pl, st);
     auto kern = moe_decode_kernel<FMT>;
     static thread_local int smem_set[64] = {};  // per device: largest opt-in already applied
     int dev = 0;
@@ -632,6 +768,11 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     }
     eng->num_sms = prop.multiProcessorCount;
     if (const char* v = std::getenv("MOE_GEMM_MIN_TOKENS")) eng->gemm_min_tokens = std::atoll(v);
+    if (const char* v = std::getenv("MOE_DIST_REQUANT_MIN")) eng->dist_min_blocks = std::atoi(v);
+    if (const char* v = std::getenv("MOE_DECODE_FLAGS")) eng->decode_flags = std::atoi(v);
+    if (const char* v = std::getenv("MOE_DECODE_SK")) eng->use_sk = std::atoi(v) != 0;
+    if (const char* v = std::getenv("MOE_SK_COST_A")) eng->sk_cost_a = std::max(0, std::atoi(v));
+    if (const char* v = std::getenv("MOE_SK_MIN_CHUNKS")) eng->sk_min_chunks_per_cta = std::max(0, std::atoi(v));
     eng->max_smem = (int)prop.sharedMemPerBlockOptin;
     int rc = MOE_OK;
     rc = alloc_q_layout(eng);
@@ -651,8 +792,9 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     DeviceGuard g(eng->cfg.device);
     cudaFree(eng->gu);
     cudaFree(eng->dn);
+    cudaFree(eng->dk);
+    cudaFree(eng->part);
     cudaFree(eng->h_ws);
-    cudaFree(eng->hmax);
     cudaFree(eng->bar);
     cudaFree(eng->timeline);
     cudaFree(eng->gws);
@@ -692,6 +834,7 @@ extern "C" int moe_engine_load_quantized(moe_engine* eng, const void* gu_qs, con
         CUDA_TRY(cudaGetLastError());
         if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
     }
+    if (int rc = build_down_chunks(eng, 0, E, st)) return rc;
     CUDA_TRY(cudaStreamSynchronize(st));
     eng->scale_bf16 = scale_dtype == MOE_BF16;
     eng->loaded = true;
@@ -733,6 +876,8 @@ extern "C" int moe_engine_quantize_store_expert(moe_engine* eng, int64_t expert,
                                                                                        sb, stride);
     CUDA_TRY(cudaGetLastError());
     if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
+    if (proj == 2)
+        if (int rc = build_down_chunks(eng, expert, expert + 1, st)) return rc;
     CUDA_TRY(cudaStreamSynchronize(st));
     eng->scale_bf16 = 0;
     eng->loaded = true;
@@ -790,6 +935,8 @@ extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t t
         GemmWs w;
         if (int rc = gemm_workspace(eng, max_tokens, top_k, w)) return rc;
     }
+    if (eng->dk)
+        if (int rc = ensure_part(eng, std::min<int64_t>(max_tokens, 64))) return rc;
     return ensure_workspace(eng, std::min<int64_t>(max_tokens, 64) * top_k);
 }
 
@@ -806,7 +953,7 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     DeviceGuard g(eng->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (T == 0) return MOE_OK;
-    const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    const int64_t H = eng->cfg.hidden_size;
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
     if (T > eng->gemm_min_tokens && gemm_path_ok(eng)) {  // dense enough for the grouped GEMMs
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -825,18 +972,27 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         return MOE_OK;
     }
     // token slice that fits the decode kernel's shared-memory plan
+    // (the split-K kernel when its plan fits)
+    auto plan = [&](int n, DecodePlan& pl) {
+        return plan_decode_sk(eng, n, (int)K, pl) || plan_decode(eng, n, (int)K, pl);
+    };
     int64_t slice = T;
     DecodePlan pl;
-    while (slice > 0 && !plan_decode(eng, (int)slice, (int)K, pl)) slice = slice > 8 ? slice / 2 : slice - 1;
+    while (slice > 0 && !plan((int)slice, pl)) slice = slice > 8 ? slice / 2 : slice - 1;
     if (slice == 0) return fail(MOE_ERR_INVALID, "shapes exceed the decode kernel's shared memory");
-    if (int rc = ensure_workspace(eng, slice * K)) return rc;
+    if (pl.sk) {
+        if (int rc = ensure_part(eng, slice)) return rc;
+    } else if (int rc = ensure_workspace(eng, slice * K)) {
+        return rc;
+    }
+    if (int rc = ensure_workspace(eng, 1)) return rc;  // barrier counter and error word
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     CUDA_TRY(cudaStreamIsCapturing(st, &cap));
     const bool timed = cap == cudaStreamCaptureStatusNone;
     if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
     for (int64_t t0 = 0; t0 < T; t0 += slice) {
         const int64_t n = std::min(slice, T - t0);
-        if (n != slice && !plan_decode(eng, (int)n, (int)K, pl)) return fail(MOE_ERR_INVALID, "plan failed");
+        if (n != slice && !plan((int)n, pl)) return fail(MOE_ERR_INVALID, "plan failed");
         DecodeParams& p = pl.p;
         p.T = (int)n;
         p.act_bf16 = act_dtype == MOE_BF16;
@@ -847,8 +1003,7 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         p.tw = topk_w + t0 * K;
         p.gu = eng->gu; p.dn = eng->dn;
         p.h_ws = eng->h_ws; p.bar = reinterpret_cast<unsigned long long*>(eng->bar); p.err = eng->err;
-        p.hmax = eng->hmax;
-        p.hmax_stride = (int32_t)(eng->h_cap * (I / 32));
+        p.dk = eng->dk; p.part = eng->part;
         p.dbg = eng->timeline;
         const int qt = eng->cfg.quant_type;
         const int rc = qt == MOE_Q4_0 ? launch_decode<kQ4>(pl, st)
@@ -883,11 +1038,7 @@ extern "C" int moe_engine_device_error(moe_engine* eng, int32_t* code) {
     int32_t v = 0;
     CUDA_TRY(cudaMemcpy(&v, eng->err, 4, cudaMemcpyDeviceToHost));
     *code = v;
-    if (v != 0) {  // clear the error word, the barrier state and the block maxima
-        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
-        if (eng->hmax)
-            CUDA_TRY(cudaMemset(eng->hmax, 0, 2 * (size_t)eng->h_cap * (eng->cfg.intermediate_size / 32) * 4));
-    }
+    if (v != 0) CUDA_TRY(cudaMemset(eng->bar, 0, 256));  // clear the error word and the barrier state
     return MOE_OK;
 }
 
@@ -999,9 +1150,9 @@ extern "C" int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64
 // runtimes that reserve all device memory up front and forbid allocations
 // afterwards, or latency-critical paths where an allocation (which may
 // synchronise the device) is not acceptable.  moe_engine_forward_noalloc runs the
-// same fused decode kernel as moe_engine_forward but takes its scratch (the h
-// workspace, the per-block maxima, the grid-barrier counter and the error word)
-// from the fixed device array below instead of the engine's workspace, so it
+// fused decode kernel with the grid barrier between gate_up and down (the one
+// moe_engine_forward uses for AWQ) but takes its scratch (the h workspace, the
+// grid-barrier counter and the error word) from the fixed device array below instead of the engine's workspace, so it
 // allocates nothing.  The array lives in every GPU that loads this library until
 // the process exits.
 constexpr size_t kNoAllocScratchBytes = 512 * 1024;
@@ -1040,23 +1191,22 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
     if (T > 0 && (!x || !y || !topk_ids || !topk_w)) return fail(MOE_ERR_INVALID, "null tensor pointer");
     const int64_t I = eng->cfg.intermediate_size;
     const int64_t P = T * K;
-    const int64_t hm_entries = P * (I / 32);
-    const size_t need = kNoAllocHeader + (size_t)2 * hm_entries * 4 + (size_t)P * I * 4;
+    const size_t need = kNoAllocHeader + (size_t)8 * P * (I / 32) + (size_t)P * I * 4;
     if (need > kNoAllocScratchBytes)
         return fail(MOE_ERR_INVALID, "num_tokens x top_k x intermediate_size needs " + std::to_string(need) +
                                          " bytes of scratch; moe_engine_forward_noalloc holds at most " +
                                          std::to_string(kNoAllocScratchBytes));
     DeviceGuard g(eng->cfg.device);
     if (T == 0) return MOE_OK;
-    DecodePlan pl;
+    DecodePlan pl;  // the barrier-in-the-middle kernel: its scratch does not grow with the grid
     if (!plan_decode(eng, (int)T, (int)K, pl))
         return fail(MOE_ERR_INVALID, "num_tokens x top_k too large for one decode launch; use moe_engine_forward");
     unsigned char* base = nullptr;
     if (int rc = noalloc_scratch(eng->cfg.device, &base)) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // every call reuses the array: clear the barrier counter, the error word and both
-    // block-maxima buffers (they must start at zero), leave h to be overwritten
-    CUDA_TRY(cudaMemsetAsync(base, 0, kNoAllocHeader + (size_t)2 * hm_entries * 4, st));
+    // every call reuses the array: clear the barrier counter and the error word (they
+    // must start at zero), leave h to be overwritten
+    CUDA_TRY(cudaMemsetAsync(base, 0, kNoAllocHeader, st));
     DecodeParams& p = pl.p;
     p.act_bf16 = act_dtype == MOE_BF16;
     p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
@@ -1068,9 +1218,7 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
     p.dn = eng->dn;
     p.bar = reinterpret_cast<unsigned long long*>(base);
     p.err = reinterpret_cast<int32_t*>(base + 64);
-    p.hmax = reinterpret_cast<uint32_t*>(base + kNoAllocHeader);
-    p.hmax_stride = (int32_t)hm_entries;
-    p.h_ws = reinterpret_cast<float*>(base + kNoAllocHeader + (size_t)2 * hm_entries * 4);
+    p.h_ws = reinterpret_cast<float*>(base + kNoAllocHeader + (size_t)8 * P * (I / 32));
     p.dbg = nullptr;
     const int qt = eng->cfg.quant_type;
     return qt == MOE_Q4_0 ? launch_decode<kQ4>(pl, st)

@@ -10,10 +10,9 @@
 //   phase 1  gate_up: the U*I units (gate row j + up row j of an active expert)
 //            are split into equal contiguous ranges, one per CTA, dealt to its
 //            warps round-robin; a unit's rows are dotted with the expert's token
-//            rows, SiLU(gate)*up goes to the fp32 workspace h[pos][j] and |h| is
-//            max-reduced per 32-block into hmax (global atomics);
+//            rows, SiLU(gate)*up goes to the fp32 workspace h[pos][j];
 //   barrier  one grid barrier (bounded spin);
-//   phase 2  every CTA requantises h with the block maxima (pack_A_q8_0,
+//   phase 2  every CTA requantises h, one thread per 32-block (pack_A_q8_0,
 //            gemm_kernels.cpp:394-425), computes the down rows [n0,n1) it owns for
 //            ALL active experts and then the k-ordered combine
 //            y[t][n] = sum_k w[t,k] out[pos(t,k)][n] (q8_gemm.cpp:593-613).
@@ -31,9 +30,14 @@ namespace moe {
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTokTile = 4;  // token rows held in registers per pass
-constexpr int kStamps = 16;
+constexpr int kStamps = 20;
 
 enum Fmt : int { kQ8 = 0, kQ4 = 1, kAWQ = 2 };
+// kFlagEvictFirst: weight copies carry an L2 evict-first policy, so the streamed weights do
+//   not displace what every launch re-reads (kernel code, tokens, routing, h, the barrier).
+// kFlagLateDown: a warp issues its first down-row copy only after its first gate_up item
+//   has arrived, so the gate_up bytes (on the critical path) are not queued behind them.
+constexpr int kFlagEvictFirst = 1, kFlagLateDown = 2;
 
 struct DecodeParams {
     // gate_up unit records [E][I]: gate qs row j (rs1) | up qs row j (rs1) | gate scales (ss1) | up scales (ss1)
@@ -48,8 +52,8 @@ struct DecodeParams {
     const int32_t* ids;
     const float* tw;
     float* h_ws;         // [T*K][I]
-    uint32_t* hmax;      // [2][hmax_stride]  |h| maxima per (pos, 32-block), double buffered
-    int32_t hmax_stride; // entries per buffer (>= T*K*I/32)
+    const uint8_t* dk;   // split-K kernel: down chunks [E][I/32][H/32] x (32 rows x BB | 32 scales)
+    float* part;         // split-K kernel: per-CTA fp32 partial tiles [grid][T][H]
     unsigned long long* bar;  // grid barrier arrival counter (monotonic)
     int32_t* err;        // device error word
     // shared-memory carve-up (bytes)
@@ -58,6 +62,9 @@ struct DecodeParams {
     int32_t lanes_per_row;  // phase-2 lanes per down row (power of two)
     int32_t units_per_item; // phase-1 gate/up units per bulk copy (1, 2 or 4)
     int32_t group;          // AWQ group size along K (multiple of 32)
+    int32_t dist_min_blocks;  // Q8/Q4: requantise h before the grid barrier when U*I/32 >= this
+    int32_t flags;            // kFlagEvictFirst | kFlagLateDown
+    int32_t sk_cost_a;        // split-K kernel: cost of streaming one chunk, in units of one token's compute
     unsigned long long* dbg;  // optional per-CTA phase stamps [grid][kStamps] (globaltimer ns)
 };
 
@@ -240,24 +247,110 @@ MOE_DEV void quant_x_smem(const uint8_t* x, int act_bf16, int nrows, int cols, i
     }
 }
 
-// Requantise h [P][I] (fp32, global) with the per-block maxima `hmax`, one
-// thread per 32-block: the scale needs no reduction (pack_A_q8_0 rule).
+// One 32-block of h quantised by a quad of lanes (sub = lane & 3 holds elements
+// 8sub..8sub+7 in v and writes output bytes 8sub..8sub+7): the quad reduces the
+// maximum and the sum with shuffles, so the result equals the one-thread rule of
+// pack_A_q8_0 (max and integer sum do not depend on the order).  For Q4 the byte
+// order is the permuted activation order (word 2sub: elements 8sub+{0,2,4,6},
+// word 2sub+1: 8sub+{1,3,5,7}); for Q8 it is the natural order.
 template <bool Q4>
-MOE_DEV void requant_h_smem(const float* h, const uint32_t* hmax, int P, int I, int8_t* q, float* d, int32_t* s,
-                            int tid) {
-    const int nblk = P * (I >> 5);
-    for (int g = tid; g < nblk; g += kThreads) {
-        const float4* src = reinterpret_cast<const float4*>(h + (size_t)g * 32);
-        float v[32];
+MOE_DEV void quad_quant(const float (&v)[8], uint32_t qmask, float& d, int& sum, uint2& out) {
+    float amax = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float4 f = __ldcg(src + k);
-            v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(qmask, amax, 2));
+    d = q8_scale(amax);
+    const float id = q8_inv(d);
+    int q[8];
+    sum = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        q[e] = q8_quant(v[e], id);
+        sum += q[e];
+    }
+    sum += __shfl_xor_sync(qmask, sum, 1);
+    sum += __shfl_xor_sync(qmask, sum, 2);
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        w0 |= (uint32_t)(q[Q4 ? 2 * i : i] & 0xff) << (8 * i);
+        w1 |= (uint32_t)(q[Q4 ? 2 * i + 1 : 4 + i] & 0xff) << (8 * i);
+    }
+    out = make_uint2(w0, w1);
+}
+
+MOE_DEV uint32_t quad_mask(int lane) { return 0xfu << (lane & ~3); }
+
+MOE_DEV void load8(const float* src, float (&v)[8]) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Requantise all of h [P][I] (fp32, global) into shared memory, a quad per 32-block.
+template <bool Q4>
+MOE_DEV void requant_h_smem(const float* h, int P, int I, int8_t* q, float* d, int32_t* s, int tid) {
+    const int nblk = P * (I >> 5), sub = tid & 3;
+    const uint32_t qm = quad_mask(tid & 31);
+    for (int g = tid >> 2; g < nblk; g += kThreads / 4) {
+        float v[8];
+        load8(h + (size_t)g * 32 + sub * 8, v);
+        float dd;
+        int sum;
+        uint2 o;
+        quad_quant<Q4>(v, qm, dd, sum, o);
+        *reinterpret_cast<uint2*>(q + (size_t)g * 32 + sub * 8) = o;
+        if (sub == 0) {
+            d[g] = dd;
+            if (Q4) s[g] = sum;
         }
-        const float dd = q8_scale(__uint_as_float(__ldcg(hmax + g)));
-        const int sum = quant_block_store<Q4>(v, dd, q + (size_t)g * 32);
-        d[g] = dd;
-        if (Q4) s[g] = sum;
+    }
+}
+
+// Before the grid barrier: this CTA requantises the 32-blocks [bb, be) of the
+// unique-expert x I unit space that its own phase 1 produced, in place: the
+// 128-byte fp32 slot h[pos][32jb..32jb+31] becomes q (32 B) | d (4 B) | sum (4 B).
+// Only the owning quad reads and writes a slot, so the overwrite is race free.
+template <bool Q4>
+MOE_DEV void requant_own_blocks(float* h, const RouteSmem& rt, int I, int nb2, int bb, int be, int tid) {
+    const int sub = tid & 3;
+    const uint32_t qm = quad_mask(tid & 31);
+    int t = tid >> 2;
+    for (int u = bb / nb2; u * nb2 < be; ++u) {
+        const int jb0 = max(bb, u * nb2) - u * nb2, jb1 = min(be, (u + 1) * nb2) - u * nb2;
+        const int nj = jb1 - jb0, n = nj * rt.ucnt[u];
+        for (; t < n; t += kThreads / 4) {
+            const int m = t / nj, jb = jb0 + (t - m * nj);
+            float* slot = h + (size_t)(rt.ups[u] + m) * I + jb * 32;
+            float v[8];
+            load8(slot + sub * 8, v);
+            float dd;
+            int sum;
+            uint2 o;
+            quad_quant<Q4>(v, qm, dd, sum, o);  // every lane's loads precede the shuffles, hence the stores
+            uint8_t* sb = reinterpret_cast<uint8_t*>(slot);
+            *reinterpret_cast<uint2*>(sb + sub * 8) = o;
+            if (sub == 0) *reinterpret_cast<float2*>(sb + 32) = make_float2(dd, __int_as_float(sum));
+        }
+        t -= n;
+    }
+}
+
+// After the grid barrier: gather the requantised slots of every position into
+// shared memory (q [P][I], d and sum [P][I/32]).
+template <bool Q4>
+MOE_DEV void gather_h_smem(const float* h, int P, int I, int8_t* q, float* d, int32_t* s, int tid) {
+    const int nb2 = I >> 5, nblk = P * nb2;
+    for (int g = tid >> 1; g < nblk; g += kThreads / 2) {  // a lane pair per slot
+        const uint8_t* sb = reinterpret_cast<const uint8_t*>(h + (size_t)g * 32);
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(sb) + (tid & 1));
+        const float2 ds = (tid & 1) ? __ldcg(reinterpret_cast<const float2*>(sb + 32)) : make_float2(0.f, 0.f);
+        *reinterpret_cast<uint4*>(q + (size_t)g * 32 + (tid & 1) * 16) = v;
+        if (tid & 1) {
+            d[g] = ds.x;
+            if (Q4) s[g] = __float_as_int(ds.y);
+        }
     }
 }
 
@@ -350,32 +443,31 @@ MOE_DEV void awq_sz(const uint8_t* sc, int b, int blocks_per_group, int ngroups,
 // nibbles) against 32 int8 activations (Q4: permuted, bias 8 via asum).
 template <bool Q4>
 MOE_DEV int block_dot(const uint4* w, const uint4* a, int asum) {
+    // four independent dp4a chains (integer sums: the order does not change the result)
     if (Q4) {
         const uint4 ww = w[0];
         const uint4 a0 = a[0], a1 = a[1];
-        int s = 0;
-        s = __dp4a((int)(ww.x & 0x0f0f0f0fu), (int)a0.x, s);
-        s = __dp4a((int)((ww.x >> 4) & 0x0f0f0f0fu), (int)a0.y, s);
-        s = __dp4a((int)(ww.y & 0x0f0f0f0fu), (int)a0.z, s);
-        s = __dp4a((int)((ww.y >> 4) & 0x0f0f0f0fu), (int)a0.w, s);
-        s = __dp4a((int)(ww.z & 0x0f0f0f0fu), (int)a1.x, s);
-        s = __dp4a((int)((ww.z >> 4) & 0x0f0f0f0fu), (int)a1.y, s);
-        s = __dp4a((int)(ww.w & 0x0f0f0f0fu), (int)a1.z, s);
-        s = __dp4a((int)((ww.w >> 4) & 0x0f0f0f0fu), (int)a1.w, s);
-        return s - 8 * asum;
+        int s0 = __dp4a((int)(ww.x & 0x0f0f0f0fu), (int)a0.x, 0);
+        int s1 = __dp4a((int)(ww.y & 0x0f0f0f0fu), (int)a0.z, 0);
+        int s2 = __dp4a((int)(ww.z & 0x0f0f0f0fu), (int)a1.x, 0);
+        int s3 = __dp4a((int)(ww.w & 0x0f0f0f0fu), (int)a1.z, 0);
+        s0 = __dp4a((int)((ww.x >> 4) & 0x0f0f0f0fu), (int)a0.y, s0);
+        s1 = __dp4a((int)((ww.y >> 4) & 0x0f0f0f0fu), (int)a0.w, s1);
+        s2 = __dp4a((int)((ww.z >> 4) & 0x0f0f0f0fu), (int)a1.y, s2);
+        s3 = __dp4a((int)((ww.w >> 4) & 0x0f0f0f0fu), (int)a1.w, s3);
+        return (s0 + s1) + (s2 + s3) - 8 * asum;
     } else {
         const uint4 w0 = w[0], w1 = w[1];
         const uint4 a0 = a[0], a1 = a[1];
-        int s = 0;
-        s = __dp4a((int)w0.x, (int)a0.x, s);
-        s = __dp4a((int)w0.y, (int)a0.y, s);
-        s = __dp4a((int)w0.z, (int)a0.z, s);
-        s = __dp4a((int)w0.w, (int)a0.w, s);
-        s = __dp4a((int)w1.x, (int)a1.x, s);
-        s = __dp4a((int)w1.y, (int)a1.y, s);
-        s = __dp4a((int)w1.z, (int)a1.z, s);
-        s = __dp4a((int)w1.w, (int)a1.w, s);
-        return s;
+        int s0 = __dp4a((int)w0.x, (int)a0.x, 0);
+        int s1 = __dp4a((int)w0.y, (int)a0.y, 0);
+        int s2 = __dp4a((int)w0.z, (int)a0.z, 0);
+        int s3 = __dp4a((int)w0.w, (int)a0.w, 0);
+        s0 = __dp4a((int)w1.x, (int)a1.x, s0);
+        s1 = __dp4a((int)w1.y, (int)a1.y, s1);
+        s2 = __dp4a((int)w1.z, (int)a1.z, s2);
+        s3 = __dp4a((int)w1.w, (int)a1.w, s3);
+        return (s0 + s1) + (s2 + s3);
     }
 }
 
@@ -403,20 +495,25 @@ struct P2Work {
     int n2, ngrp, RPG, R, n0;
 };
 
-MOE_DEV void issue_p1(const DecodeParams& p, const RouteSmem& rt, int u, int j0, int n, uint8_t* slot, uint64_t* bar) {
+MOE_DEV void issue_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    mbar_arrive_expect_tx(bar, bytes);
+    if (pol) bulk_g2s_hint(dst, src, bytes, bar, pol);
+    else bulk_g2s(dst, src, bytes, bar);
+}
+
+MOE_DEV void issue_p1(const DecodeParams& p, const RouteSmem& rt, int u, int j0, int n, uint8_t* slot, uint64_t* bar,
+                      uint64_t pol) {
     const uint32_t ub = 2u * (p.rs1 + p.ss1);
-    mbar_arrive_expect_tx(bar, ub * n);
-    bulk_g2s(slot, p.gu + ((size_t)rt.ue[u] * p.I + j0) * ub, ub * n, bar);
+    issue_copy(slot, p.gu + ((size_t)rt.ue[u] * p.I + j0) * ub, ub * n, bar, pol);
 }
 
 MOE_DEV void issue_p2(const DecodeParams& p, const RouteSmem& rt, const P2Work& w2, int it, uint8_t* slot,
-                      uint64_t* bar) {
+                      uint64_t* bar, uint64_t pol) {
     const int ui = it / w2.ngrp, g = it - ui * w2.ngrp;
     const int r0 = g * w2.RPG;
     const int rows = min(w2.RPG, w2.R - r0);
     const uint32_t rb = (uint32_t)(p.rs2 + p.ss2);
-    mbar_arrive_expect_tx(bar, rows * rb);
-    bulk_g2s(slot, p.dn + ((size_t)rt.ue[ui] * p.H + w2.n0 + r0) * rb, rows * rb, bar);
+    issue_copy(slot, p.dn + ((size_t)rt.ue[ui] * p.H + w2.n0 + r0) * rb, rows * rb, bar, pol);
 }
 
 template <int FMT>
@@ -450,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
         route_warp(p.ids, TK, E, p.e_off, rt, lane);
         if (lane == 0) {
             s_ok = 1;
-            s_launch = barrier_launch_index(p.bar, (uint32_t)G);  // selects this launch's hmax buffer
+            s_launch = barrier_launch_index(p.bar, (uint32_t)G);  // this launch's barrier target
             if (dbg) dbg[1] = global_ns();
         }
     } else {
@@ -467,12 +564,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
 
     const int U = *rt.nuniq;
     const unsigned long long launch = s_launch;
-    const uint32_t par = (uint32_t)(launch & 1ull);
-    uint32_t* hmax = p.hmax + (size_t)par * p.hmax_stride;
 
-    // this warp's phase-1 share and phase-2 items
+    // this warp's phase-1 share and phase-2 items; in the distributed-requant mode a
+    // CTA owns whole 32-blocks of units so it can requantise them itself
     const int64_t TU = (int64_t)U * I;
-    const int64_t cb = TU * cta / G, ce = TU * (cta + 1) / G;
+    const int NB = U * nb2;
+    const bool dist = !AWQ && NB >= p.dist_min_blocks;
+    const int bb = (int)((int64_t)NB * cta / G), be = (int)((int64_t)NB * (cta + 1) / G);
+    const int64_t cb = dist ? (int64_t)bb * 32 : TU * cta / G, ce = dist ? (int64_t)be * 32 : TU * (cta + 1) / G;
     P1Cursor c_issue{cb + (ce - cb) * warp / kWarps, cb + (ce - cb) * (warp + 1) / kWarps, I, p.units_per_item};
     P1Cursor c_use = c_issue;
     P2Work w2;
@@ -483,40 +582,36 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     const int tot2 = U * w2.ngrp;
     w2.n2 = warp < tot2 ? (tot2 - warp + kWarps - 1) / kWarps : 0;
     int issued2 = 0;  // phase-2 items issued so far
+    int nissued = 0;  // items issued so far; item k sits in ring slot k % slots
+    const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
 
-    // issue the first `slots` items (phase 1, then phase 2) of this warp
-    int n_inflight = 0;
-    if (lane == 0) {
-        int u, j0, n;
-        while (n_inflight < p.slots && c_issue.next(u, j0, n)) {
-            issue_p1(p, rt, u, j0, n, myring + (size_t)n_inflight * p.slot_bytes, &mybar[n_inflight]);
-            ++n_inflight;
-        }
-        while (n_inflight < p.slots && issued2 < w2.n2) {
-            issue_p2(p, rt, w2, warp + issued2 * kWarps, myring + (size_t)n_inflight * p.slot_bytes, &mybar[n_inflight]);
-            ++issued2;
-            ++n_inflight;
-        }
-    }
-    // lane 0 advances its cursors; keep the other lanes' copies in step
-    c_issue.cur = __shfl_sync(0xffffffffu, c_issue.cur, 0);
-    issued2 = __shfl_sync(0xffffffffu, issued2, 0);
-
-    auto refill = [&](int s) {  // after consuming slot s: issue this warp's next item into it
-        __syncwarp();  // every lane's reads of slot s are complete before lane 0 reuses it
+    // lane 0 fills the free ring slots (items are consumed in issue order): phase-1
+    // items first, then phase-2 items when allowed
+    auto top_up = [&](int consumed, bool allow_p2) {
+        __syncwarp();  // every lane's reads of the consumed slots are complete before reuse
         if (lane == 0) {
-            int u, j0, n;
-            if (c_issue.next(u, j0, n)) {
-                issue_p1(p, rt, u, j0, n, myring + (size_t)s * p.slot_bytes, &mybar[s]);
-            } else if (issued2 < w2.n2) {
-                issue_p2(p, rt, w2, warp + issued2 * kWarps, myring + (size_t)s * p.slot_bytes, &mybar[s]);
-                if (dbg && warp == 0 && issued2 == 0) dbg[15] = global_ns();
-                ++issued2;
+            while (nissued - consumed < p.slots) {
+                const int s = nissued % p.slots;
+                int u, j0, n;
+                if (c_issue.next(u, j0, n)) {
+                    issue_p1(p, rt, u, j0, n, myring + (size_t)s * p.slot_bytes, &mybar[s], pol);
+                } else if (allow_p2 && issued2 < w2.n2) {
+                    issue_p2(p, rt, w2, warp + issued2 * kWarps, myring + (size_t)s * p.slot_bytes, &mybar[s], pol);
+                    if (dbg && warp == 0 && issued2 == 0) dbg[15] = global_ns();
+                    ++issued2;
+                } else {
+                    break;
+                }
+                ++nissued;
             }
         }
+        // lane 0 advanced the cursors; keep the other lanes' copies in step
         c_issue.cur = __shfl_sync(0xffffffffu, c_issue.cur, 0);
         issued2 = __shfl_sync(0xffffffffu, issued2, 0);
+        nissued = __shfl_sync(0xffffffffu, nissued, 0);
     };
+    top_up(0, !(p.flags & kFlagLateDown) || c_issue.cur >= c_issue.end);
+    auto refill = [&](int consumed) { top_up(consumed, true); };
 
     const bool sbf = p.scale_bf16 != 0;
     bool ok = true;
@@ -552,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
                     au[m] = 0.f;
                 }
                 if (valid) {
-#pragma unroll 2
+#pragma unroll 4
                     for (int b = usub; b < nb1; b += LPU) {
                         const uint4* wg = reinterpret_cast<const uint4*>(qg + (size_t)b * BB);
                         const uint4* wu = reinterpret_cast<const uint4*>(qu + (size_t)b * BB);
@@ -604,20 +699,25 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
                     const float hv = silu_mul(g, uu);
                     const int pos = ps + m0 + usub;
                     p.h_ws[(size_t)pos * I + j] = hv;
-                    if constexpr (!AWQ) atomicMax(hmax + (size_t)pos * nb2 + (j >> 5), __float_as_uint(fabsf(hv)));
                 }
             }
-            refill(s);
             ++item;
+            refill(item);
         }
     }
     if (dbg && tid == 0) dbg[6] = global_ns();
 
     // ---------------- grid barrier ----------------
     __syncthreads();
+    if constexpr (!AWQ) {
+        if (dist && ok) {
+            requant_own_blocks<Q4>(p.h_ws, rt, I, nb2, bb, be, tid);
+            __syncthreads();
+        }
+    }
     if (dbg && tid == 0) dbg[7] = global_ns();
     if (tid == 1) {  // a lane that issues no bulk copies: its release waits on no copy in flight
-        if (!grid_barrier(p.bar, (uint32_t)G, (launch + 1ull) * (uint32_t)G, p.err)) s_ok = 0;
+        if (!grid_barrier(p.bar, (uint32_t)G, (launch + 1ull) * (uint32_t)G, p.err, dbg ? dbg + 16 : nullptr)) s_ok = 0;
     }
     __syncthreads();
     ok = ok && s_ok;
@@ -633,12 +733,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     float* hsum = hf + (size_t)P * I;                              // AWQ: per-block sums
     if (ok && w2.R > 0 && U > 0) {
         if constexpr (AWQ) stage_h_awq(p.h_ws, P, I, hf, hsum, tid);
-        else requant_h_smem<Q4>(p.h_ws, hmax, P, I, hq, hd, hs, tid);
-    }
-    {   // clear the other hmax buffer for the next launch (no CTA reads it in this launch)
-        uint32_t* other = p.hmax + (size_t)(par ^ 1u) * p.hmax_stride;
-        if constexpr (!AWQ)
-            for (int i = cta * kThreads + tid; i < p.hmax_stride; i += G * kThreads) other[i] = 0u;
+        else if (dist) gather_h_smem<Q4>(p.h_ws, P, I, hq, hd, hs, tid);
+        else requant_h_smem<Q4>(p.h_ws, P, I, hq, hd, hs, tid);
     }
     __syncthreads();
     if (dbg && tid == 0) dbg[9] = global_ns();
@@ -647,6 +743,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     const int sub = lane % LPR, rr = lane / LPR;
     for (int k2 = 0; ok && k2 < w2.n2; ++k2) {
         const int s = item % p.slots;
+        if (dbg && tid == 0 && k2 == 0) dbg[19] = global_ns();
         if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
         if (dbg && tid == 0 && k2 == 0) dbg[10] = global_ns();
         const uint8_t* st = myring + (size_t)s * p.slot_bytes;
@@ -700,12 +797,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
                     if (m < nt) outs[(size_t)(ps + m0 + m) * p.rows_max + row] = acc[m];
             }
         }
-        refill(s);
         ++item;
+        refill(item);
     }
+    if (dbg && tid == 0) dbg[18] = global_ns();
     // drain: a warp that stopped early still waits (bounded) for its copies in flight
     if (!ok && lane == 0)
-        for (int i = item; i < item + p.slots; ++i) mbar_wait(&mybar[i % p.slots], (uint32_t)(i / p.slots) & 1u);
+        for (int i = item; i < nissued; ++i) mbar_wait(&mybar[i % p.slots], (uint32_t)(i / p.slots) & 1u);
     __syncthreads();
     if (dbg && tid == 0) dbg[11] = global_ns();
     if (!ok) return;

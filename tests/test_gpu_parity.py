@@ -245,3 +245,17 @@ def test_gemm_and_decode_paths_agree(monkeypatch):
         outs.append(y)
     rel, cos = parity(outs[0], outs[1])
     assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
+
+
+@pytest.mark.parametrize("qt,E,H,I,T,K", [(0, 16, 512, 256, 3, 8), (1, 64, 2048, 768, 8, 8), (1, 128, 2048, 768, 1, 8)])
+def test_split_k_kernel_matches_barrier_kernel(qt, E, H, I, T, K, monkeypatch):
+    # the split-K decode kernel (default for Q8_0/Q4_0) against the kernel with the grid
+    # barrier between gate_up and down: both within fp32 rounding of each other
+    monkeypatch.setenv("MOE_SK_MIN_CHUNKS", "0")  # split-K even where the default picks the barrier kernel
+    y_sk, y_ref, _ = run_engine(qt, E, H, I, T, K, seed=31, out_dtype=capi.F32)
+    monkeypatch.setenv("MOE_DECODE_SK", "0")
+    y_bar, _, _ = run_engine(qt, E, H, I, T, K, seed=31, out_dtype=capi.F32)
+    rel, cos = parity(y_sk, y_bar)
+    assert rel <= 1e-5 and cos >= 0.999999, (rel, cos)
+    rel, cos = parity(y_sk, y_ref)
+    assert rel <= 2e-3 and cos >= MIN_COS, (rel, cos)
