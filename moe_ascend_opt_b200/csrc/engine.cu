@@ -67,8 +67,9 @@ struct moe_engine {
     int32_t* err = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     bool timed = false;
-    int64_t gemm_min_tokens = 32;  // forwards with more tokens take the grouped-GEMM path
+    int64_t gemm_min_tokens = 16;  // forwards with more tokens take the grouped-GEMM path
     int32_t decode_flags = kFlagEvictFirst;
+    int32_t gemm_bm = 0;  // grouped-GEMM token rows per tile (16, 32, 64); 0 = by tokens per expert
     int32_t dist_min_blocks = -1;  // decode: requantise h before the barrier from this many blocks (-1: 2 x SMs)
     // grouped-GEMM path workspace (one allocation, carved per call)
     uint8_t* gws = nullptr;
@@ -670,6 +671,41 @@ int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
     return MOE_OK;
 }
 
+// Token rows per GEMM tile: the expected tokens per active expert (uniform routing)
+// picks the smallest tile that is not mostly padding.
+int gemm_tile_rows(const moe_engine* eng, int64_t TK) {
+    if (eng->gemm_bm) return eng->gemm_bm;
+    const int64_t per_expert = TK / std::max<int64_t>(1, std::min<int64_t>(eng->cfg.num_experts, TK));
+    return per_expert <= 16 ? 16 : (per_expert <= 40 ? 32 : 64);
+}
+
+template <bool Q4, int BM>
+int launch_gemms(moe_engine* eng, const gemm::GemmParams& g1, const gemm::GemmParams& g2, int64_t TK,
+                 cudaStream_t st) {
+    using S = gemm::Stage<Q4, BM>;
+    const int smem = std::max(gemm::kStages * S::kBytes, BM * (gemm::kBN / 2 + 1) * 4);
+    static thread_local int smem_set[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    const int64_t mt_bound = (TK + BM - 1) / BM + std::min<int64_t>(E, TK);
+    auto k1 = gemm::grouped_gemm_kernel<Q4, true, BM>;
+    auto k2 = gemm::grouped_gemm_kernel<Q4, false, BM>;
+    if (dev < 64 && smem_set[1][dev] < smem) {
+        CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        smem_set[1][dev] = smem;
+    }
+    if (dev < 64 && smem_set[0][dev] < smem) {
+        CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        smem_set[0][dev] = smem;
+    }
+    k1<<<(unsigned)(mt_bound * (2 * I / gemm::kBN)), gemm::kThreads, smem, st>>>(g1);
+    CUDA_TRY(cudaGetLastError());
+    k2<<<(unsigned)(mt_bound * (H / gemm::kBN)), gemm::kThreads, smem, st>>>(g2);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
 template <bool Q4>
 int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, const float* tw, int64_t T, int64_t K,
                    int act_bf16, int out_kind, cudaStream_t st) {
@@ -681,7 +717,7 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     const int eoff = eng->cfg.expert_offset;
     gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk);
     gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
-                                                                                  w.mtile);
+                                                                                  w.mtile, gemm_tile_rows(eng, TK));
     gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk, w.starts, w.smap, w.tokmap);
     {
         const int nb = (int)(T * (H / 32));
@@ -689,12 +725,6 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
             static_cast<const uint8_t*>(x), act_bf16, (int)T, H, w.xq, w.xd, w.xs);
     }
     CUDA_TRY(cudaGetLastError());
-    using S = gemm::Stage<Q4>;
-    const int smem = std::max(gemm::kStages * S::kBytes, gemm::kBM * (gemm::kBN / 2 + 1) * 4);
-    static thread_local int smem_set[2][2][64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int64_t mt_bound = (TK + gemm::kBM - 1) / gemm::kBM + std::min(E, TK);
     gemm::GemmParams gp{};
     gp.scale_bf16 = eng->scale_bf16;
     gp.counts = w.counts;
@@ -703,34 +733,20 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     gp.tokmap = w.tokmap;
     gp.topk = (int)K;
     gp.E = E;
-    {   // gate_up: A = token rows, B = unit records (2 rows each)
-        auto kern = gemm::grouped_gemm_kernel<Q4, true>;
-        if (dev < 64 && smem_set[Q4][1][dev] < smem) {
-            CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            smem_set[Q4][1][dev] = smem;
-        }
-        gemm::GemmParams g1 = gp;
-        g1.aq = w.xq; g1.ad = w.xd; g1.as = w.xs;
-        g1.wbase = eng->gu; g1.rec = eng->unit_bytes(); g1.rows_per_rec = 2; g1.rs = eng->rs1;
-        g1.sc_off = 2 * eng->rs1; g1.ss = eng->ss1; g1.nrec = I; g1.K = H; g1.N = 2 * I;
-        g1.hq = w.hq; g1.hd = w.hd; g1.hs = w.hs;
-        kern<<<(unsigned)(mt_bound * (2 * I / gemm::kBN)), gemm::kThreads, smem, st>>>(g1);
-        CUDA_TRY(cudaGetLastError());
-    }
-    {   // down: A = requantised h rows, B = down row records
-        auto kern = gemm::grouped_gemm_kernel<Q4, false>;
-        if (dev < 64 && smem_set[Q4][0][dev] < smem) {
-            CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            smem_set[Q4][0][dev] = smem;
-        }
-        gemm::GemmParams g2 = gp;
-        g2.aq = w.hq; g2.ad = w.hd; g2.as = w.hs;
-        g2.wbase = eng->dn; g2.rec = eng->row_bytes(); g2.rows_per_rec = 1; g2.rs = eng->rs2;
-        g2.sc_off = eng->rs2; g2.ss = eng->ss2; g2.nrec = H; g2.K = I; g2.N = H;
-        g2.out = w.out;
-        kern<<<(unsigned)(mt_bound * (H / gemm::kBN)), gemm::kThreads, smem, st>>>(g2);
-        CUDA_TRY(cudaGetLastError());
-    }
+    gemm::GemmParams g1 = gp;  // gate_up: A = token rows, B = unit records (2 rows each)
+    g1.aq = w.xq; g1.ad = w.xd; g1.as = w.xs;
+    g1.wbase = eng->gu; g1.rec = eng->unit_bytes(); g1.rows_per_rec = 2; g1.rs = eng->rs1;
+    g1.sc_off = 2 * eng->rs1; g1.ss = eng->ss1; g1.nrec = I; g1.K = H; g1.N = 2 * I;
+    g1.hq = w.hq; g1.hd = w.hd; g1.hs = w.hs;
+    gemm::GemmParams g2 = gp;  // down: A = requantised h rows, B = down row records
+    g2.aq = w.hq; g2.ad = w.hd; g2.as = w.hs;
+    g2.wbase = eng->dn; g2.rec = eng->row_bytes(); g2.rows_per_rec = 1; g2.rs = eng->rs2;
+    g2.sc_off = eng->rs2; g2.ss = eng->ss2; g2.nrec = H; g2.K = I; g2.N = H;
+    g2.out = w.out;
+    const int bm = gemm_tile_rows(eng, TK);
+    const int rc = bm == 16 ? launch_gemms<Q4, 16>(eng, g1, g2, TK, st)
+                            : (bm == 32 ? launch_gemms<Q4, 32>(eng, g1, g2, TK, st) : launch_gemms<Q4, 64>(eng, g1, g2, TK, st));
+    if (rc) return rc;
     {
         const int64_t total = T * (H / 4);
         gemm::combine_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, eng->num_sms * 16), 256, 0, st>>>(
@@ -770,6 +786,10 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (const char* v = std::getenv("MOE_GEMM_MIN_TOKENS")) eng->gemm_min_tokens = std::atoll(v);
     if (const char* v = std::getenv("MOE_DIST_REQUANT_MIN")) eng->dist_min_blocks = std::atoi(v);
     if (const char* v = std::getenv("MOE_DECODE_FLAGS")) eng->decode_flags = std::atoi(v);
+    if (const char* v = std::getenv("MOE_GEMM_BM")) {
+        const int bm = std::atoi(v);
+        eng->gemm_bm = (bm == 16 || bm == 32 || bm == 64) ? bm : 0;
+    }
     if (const char* v = std::getenv("MOE_DECODE_SK")) eng->use_sk = std::atoi(v) != 0;
     if (const char* v = std::getenv("MOE_SK_COST_A")) eng->sk_cost_a = std::max(0, std::atoi(v));
     if (const char* v = std::getenv("MOE_SK_MIN_CHUNKS")) eng->sk_min_chunks_per_cta = std::max(0, std::atoi(v));

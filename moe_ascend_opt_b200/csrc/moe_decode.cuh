@@ -544,10 +544,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     if (lane == 0)
         for (int s = 0; s < p.slots; ++s) mbar_init(&mybar[s], 1);
     if (warp == kWarps - 1) {  // one warp routes while the others quantise the tokens
+        // this launch's barrier target: the load is in flight while the warp routes
+        const unsigned long long launch_idx = barrier_launch_index(p.bar, (uint32_t)G);
         route_warp(p.ids, TK, E, p.e_off, rt, lane);
         if (lane == 0) {
             s_ok = 1;
-            s_launch = barrier_launch_index(p.bar, (uint32_t)G);  // this launch's barrier target
+            s_launch = launch_idx;
             if (dbg) dbg[1] = global_ns();
         }
     } else {

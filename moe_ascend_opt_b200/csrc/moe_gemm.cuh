@@ -24,11 +24,11 @@
 namespace moe {
 namespace gemm {
 
-constexpr int kBM = 64;        // token rows per CTA tile
+constexpr int kBM = 64;        // token rows per CTA tile (largest variant; 32 and 16 for few tokens per expert)
 constexpr int kBN = 128;       // weight rows per CTA tile (gate_up: 64 units x 2 rows)
 constexpr int kKB = 4;         // 32-blocks per pipeline stage (K = 128)
 constexpr int kStages = 3;
-constexpr int kThreads = 256;  // 8 warps: 2 (M) x 4 (N), 32 x 32 each
+constexpr int kThreads = 256;  // 8 warps: BM 64: 2 (M) x 4 (N) of 32 x 32; BM 32: 1 x 8 of 32 x 16; BM 16: 1 x 8 of 16 x 16
 constexpr int kRowPad = 16;    // smem row padding (bank-conflict-free fragment loads)
 
 // ------------------------------------------------------------------ routing
@@ -51,7 +51,7 @@ __global__ void route_count_kernel(const int32_t* ids, int TK, int E, int e_off,
 // One CTA of >= E threads: per-block offsets (expert-major), counts, starts, and
 // per-expert first tile index of the gate_up / down GEMM tile lists.
 __global__ void route_scan_kernel(int32_t* blk_cnt, int nblk, int E, int32_t* counts, int32_t* starts,
-                                  int32_t* mtile_start) {
+                                  int32_t* mtile_start, int bm) {
     extern __shared__ int32_t sh[];  // [2][E]
     const int e = threadIdx.x;
     int tot = 0;
@@ -62,7 +62,7 @@ __global__ void route_scan_kernel(int32_t* blk_cnt, int nblk, int E, int32_t* co
             tot += c;
         }
         sh[e] = tot;
-        sh[E + e] = (tot + kBM - 1) / kBM;
+        sh[E + e] = (tot + bm - 1) / bm;
     }
     __syncthreads();
     if (e == 0) {  // serial scan over experts (E <= a few hundred)
@@ -218,26 +218,30 @@ struct GemmParams {
 };
 
 // Shared-memory layout of one stage.
-template <bool Q4>
+template <bool Q4, int BM>
 struct Stage {
     static constexpr int kAKB = kKB * 32;               // activation bytes per row per stage
     static constexpr int kARow = kAKB + kRowPad;
     static constexpr int kBKB = kKB * (Q4 ? 16 : 32);  // weight bytes per row per stage
     static constexpr int kBRow = kBKB + kRowPad;
-    static constexpr int kA = kBM * kARow;
+    static constexpr int kA = BM * kARow;
     static constexpr int kB = kBN * kBRow;
-    static constexpr int kAd = kBM * kKB * 4;
-    static constexpr int kAs = kBM * kKB * 4;
+    static constexpr int kAd = BM * kKB * 4;
+    static constexpr int kAs = BM * kKB * 4;
     static constexpr int kBd = kBN * kKB * 2;
     static constexpr int kBytes = kA + kB + kAd + kAs + kBd;
 };
 
-template <bool Q4, bool GATE_UP>
+template <bool Q4, bool GATE_UP, int BM>
 __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams p) {
-    using S = Stage<Q4>;
+    using S = Stage<Q4, BM>;
+    constexpr int WNW = BM >= 64 ? 4 : 8;      // warps along N
+    constexpr int WR = BM / (8 / WNW);         // warp tile rows
+    constexpr int WC = kBN / WNW;              // warp tile cols
+    constexpr int MI = WR / 16, NJ = WC / 8;   // m16 / n8 tiles per warp
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp >> 2, wn = warp & 3;  // warp tile: rows wm*32.., cols wn*32..
+    const int wm = warp / WNW, wn = warp % WNW;  // warp tile: rows wm*WR.., cols wn*WC..
     const int g = lane >> 2, c = lane & 3;
 
     // ---- tile -> (expert, m tile, n tile)
@@ -253,16 +257,16 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         else hi = mid;
     }
     const int e = lo;
-    const int m0 = (mt_glob - p.mtile_start[e]) * kBM;
+    const int m0 = (mt_glob - p.mtile_start[e]) * BM;
     const int cnt = p.counts[e];
     const int pos0 = p.starts[e] + m0;
-    const int mrows = min(kBM, cnt - m0);
+    const int mrows = min(BM, cnt - m0);
     const int n0 = nt * kBN;
     const int nkb = p.K / 32;  // multiple of kKB (K % 128 == 0)
 
     // source rows of the tile's activations, resolved once (gathered through tokmap for gate_up)
-    __shared__ int64_t s_arow[kBM];
-    for (int r = tid; r < kBM; r += kThreads) {
+    __shared__ int64_t s_arow[BM];
+    for (int r = tid; r < BM; r += kThreads) {
         const int rr = min(r, max(mrows, 1) - 1);
         const int pos = pos0 + rr;
         s_arow[r] = GATE_UP ? (int64_t)(p.tokmap[pos] / p.topk) : (int64_t)pos;
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         float* sAd = reinterpret_cast<float*>(base + S::kA + S::kB);
         int32_t* sAs = reinterpret_cast<int32_t*>(base + S::kA + S::kB + S::kAd);
         uint16_t* sBd = reinterpret_cast<uint16_t*>(base + S::kA + S::kB + S::kAd + S::kAs);
-        for (int ch = tid; ch < kBM * (S::kAKB / 16); ch += kThreads) {
+        for (int ch = tid; ch < BM * (S::kAKB / 16); ch += kThreads) {
             const int r = ch / (S::kAKB / 16), cc = ch % (S::kAKB / 16);
             cp_async16(sA + r * S::kARow + cc * 16, p.aq + s_arow[r] * p.K + (int64_t)kb0 * 32 + cc * 16, r < mrows);
         }
@@ -297,7 +301,7 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
             const int n = ch / (S::kBKB / 16), cc = ch % (S::kBKB / 16);
             cp_async16(sB + n * S::kBRow + cc * 16, b_row_addr(n) + (int64_t)kb0 * (Q4 ? 16 : 32) + cc * 16, true);
         }
-        for (int r = tid; r < kBM; r += kThreads) {
+        for (int r = tid; r < BM; r += kThreads) {
             cp_async16(sAd + r * kKB, p.ad + s_arow[r] * nkb + kb0, r < mrows);
             if (Q4) cp_async16(sAs + r * kKB, p.as + s_arow[r] * nkb + kb0, r < mrows);
         }
@@ -307,11 +311,11 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         }
     };
 
-    float acc[2][4][4];
+    float acc[MI][NJ][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < MI; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < NJ; ++j)
 #pragma unroll
             for (int q = 0; q < 4; ++q) acc[i][j][q] = 0.f;
 
@@ -337,10 +341,10 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         const uint16_t* sBd = reinterpret_cast<const uint16_t*>(base + S::kA + S::kB + S::kAd + S::kAs);
 #pragma unroll 2
         for (int kb = 0; kb < kKB; ++kb) {
-            uint32_t af[2][4];
+            uint32_t af[MI][4];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int r = wm * 32 + i * 16 + g;
+            for (int i = 0; i < MI; ++i) {
+                const int r = wm * WR + i * 16 + g;
                 const uint32_t* ra = reinterpret_cast<const uint32_t*>(sA + r * S::kARow + kb * 32);
                 const uint32_t* rb = reinterpret_cast<const uint32_t*>(sA + (r + 8) * S::kARow + kb * 32);
                 af[i][0] = ra[c];
@@ -348,10 +352,10 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
                 af[i][2] = ra[4 + c];
                 af[i][3] = rb[4 + c];
             }
-            uint32_t bf[4][2];
+            uint32_t bf[NJ][2];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int n = wn * 32 + j * 8 + g;
+            for (int j = 0; j < NJ; ++j) {
+                const int n = wn * WC + j * 8 + g;
                 const uint32_t* wr = reinterpret_cast<const uint32_t*>(sB + n * S::kBRow + kb * (Q4 ? 16 : 32));
                 if (Q4) {
                     const uint32_t w0 = wr[c >> 1], w1 = wr[2 + (c >> 1)];
@@ -363,25 +367,25 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
                 }
             }
             // activation scales (rows g, g+8 of each m16) and weight scales (cols 2c, 2c+1 of each n8)
-            float da[2][2];
-            int sa[2][2];
+            float da[MI][2];
+            int sa[MI][2];
 #pragma unroll
-            for (int i = 0; i < 2; ++i)
+            for (int i = 0; i < MI; ++i)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int r = wm * 32 + i * 16 + g + h * 8;
+                    const int r = wm * WR + i * 16 + g + h * 8;
                     da[i][h] = sAd[r * kKB + kb];
                     sa[i][h] = Q4 ? sAs[r * kKB + kb] : 0;
                 }
-            float dw[4][2];
+            float dw[NJ][2];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < NJ; ++j)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) dw[j][h] = scale_to_f32(sBd[(wn * 32 + j * 8 + 2 * c + h) * kKB + kb], sbf);
+                for (int h = 0; h < 2; ++h) dw[j][h] = scale_to_f32(sBd[(wn * WC + j * 8 + 2 * c + h) * kKB + kb], sbf);
 #pragma unroll
-            for (int i = 0; i < 2; ++i)
+            for (int i = 0; i < MI; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+                for (int j = 0; j < NJ; ++j) {
                     int d[4];
                     mma_s8<Q4>(d, af[i], bf[j]);
                     // d0,d1: row g, cols 2c,2c+1; d2,d3: row g+8
@@ -401,23 +405,23 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
     if (GATE_UP) {
         // columns interleave (gate, up) per unit: col 2u = gate of unit u, 2u+1 = up.
         // Thread holds cols 2c, 2c+1 of each n8 -> one unit per (j): h = silu(gate)*up.
-        float* hsm = reinterpret_cast<float*>(smem);  // [kBM][kBN/2 + 1] fp32
+        float* hsm = reinterpret_cast<float*>(smem);  // [BM][kBN/2 + 1] fp32
         constexpr int HW = kBN / 2 + 1;
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < MI; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < NJ; ++j)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int r = wm * 32 + i * 16 + g + h * 8;
-                    const int u = (wn * 32 + j * 8 + 2 * c) >> 1;
+                    const int r = wm * WR + i * 16 + g + h * 8;
+                    const int u = (wn * WC + j * 8 + 2 * c) >> 1;
                     hsm[r * HW + u] = silu_mul(acc[i][j][2 * h], acc[i][j][2 * h + 1]);
                 }
         __syncthreads();
         // requantise per (row, 32-unit block): thread per block
         const int I = p.N / 2, nbI = I / 32;
         const int u0 = n0 / 2;
-        for (int t = tid; t < kBM * (kBN / 64); t += kThreads) {
+        for (int t = tid; t < BM * (kBN / 64); t += kThreads) {
             const int r = t / (kBN / 64), blk = t % (kBN / 64);
             if (r >= mrows) continue;
             float v[32];
@@ -457,15 +461,15 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+        for (int i = 0; i < MI; ++i)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const int r = wm * 32 + i * 16 + g + h * 8;
+                const int r = wm * WR + i * 16 + g + h * 8;
                 if (r >= mrows) continue;
                 float* orow = p.out + (int64_t)(pos0 + r) * p.N + n0;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int col = wn * 32 + j * 8 + 2 * c;
+                for (int j = 0; j < NJ; ++j) {
+                    const int col = wn * WC + j * 8 + 2 * c;
                     *reinterpret_cast<float2*>(orow + col) = make_float2(acc[i][j][2 * h], acc[i][j][2 * h + 1]);
                 }
             }

@@ -259,3 +259,13 @@ def test_split_k_kernel_matches_barrier_kernel(qt, E, H, I, T, K, monkeypatch):
     assert rel <= 1e-5 and cos >= 0.999999, (rel, cos)
     rel, cos = parity(y_sk, y_ref)
     assert rel <= 2e-3 and cos >= MIN_COS, (rel, cos)
+
+
+@pytest.mark.parametrize("bm", ["16", "32", "64"])
+@pytest.mark.parametrize("qt", [0, 1])
+def test_gemm_tile_rows_variants(qt, bm, monkeypatch):
+    # every token-tile height of the grouped GEMM, on ragged per-expert counts
+    monkeypatch.setenv("MOE_GEMM_BM", bm)
+    y, y_ref, _ = run_engine(qt, 32, 1024, 384, 90, 8, seed=7, bad_ids=True)
+    rel, cos = parity(y, y_ref)
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
