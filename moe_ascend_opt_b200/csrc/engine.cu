@@ -67,9 +67,9 @@ struct moe_engine {
     int32_t* err = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     bool timed = false;
-    int64_t gemm_min_tokens = 16;  // forwards with more tokens take the grouped-GEMM path
+    int64_t gemm_min_tokens = 8;  // forwards with more tokens take the grouped-GEMM path
     int32_t decode_flags = kFlagEvictFirst;
-    int32_t gemm_bm = 0;  // grouped-GEMM token rows per tile (16, 32, 64); 0 = by tokens per expert
+    int32_t gemm_bm = 0;  // grouped-GEMM tile kind (gemm_tile_rows codes); 0 = by tokens per expert
     int32_t dist_min_blocks = -1;  // decode: requantise h before the barrier from this many blocks (-1: 2 x SMs)
     // grouped-GEMM path workspace (one allocation, carved per call)
     uint8_t* gws = nullptr;
@@ -671,12 +671,40 @@ int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
     return MOE_OK;
 }
 
-// Token rows per GEMM tile: the expected tokens per active expert (uniform routing)
-// picks the smallest tile that is not mostly padding.
+// GEMM tile kind from the expected tokens per active expert (uniform routing): up to 24,
+// the weights-on-M kernel with 8- or 16-token tiles; above, 32- or 64-token M tiles.
+// Codes: -8 / -16 weights-on-M, 16 / 32 / 64 tokens-on-M.
 int gemm_tile_rows(const moe_engine* eng, int64_t TK) {
     if (eng->gemm_bm) return eng->gemm_bm;
     const int64_t per_expert = TK / std::max<int64_t>(1, std::min<int64_t>(eng->cfg.num_experts, TK));
-    return per_expert <= 16 ? 16 : (per_expert <= 40 ? 32 : 64);
+    return per_expert <= 6 ? -8 : (per_expert <= 24 ? -16 : (per_expert <= 40 ? 32 : 64));
+}
+
+template <bool Q4, int BT>
+int launch_gemms_wm(moe_engine* eng, const gemm::GemmParams& g1, const gemm::GemmParams& g2, int64_t TK,
+                    cudaStream_t st) {
+    using S = gemm::StageW<Q4, BT>;
+    const int smem = std::max(gemm::kStages * S::kBytes, BT * (gemm::kBN / 2 + 1) * 4);
+    static thread_local int smem_set[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    const int64_t mt_bound = (TK + BT - 1) / BT + std::min<int64_t>(E, TK);
+    auto k1 = gemm::grouped_gemm_wm_kernel<Q4, true, BT>;
+    auto k2 = gemm::grouped_gemm_wm_kernel<Q4, false, BT>;
+    if (dev < 64 && smem_set[1][dev] < smem) {
+        CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        smem_set[1][dev] = smem;
+    }
+    if (dev < 64 && smem_set[0][dev] < smem) {
+        CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        smem_set[0][dev] = smem;
+    }
+    k1<<<(unsigned)(mt_bound * (2 * I / gemm::kBN)), gemm::kThreads, smem, st>>>(g1);
+    CUDA_TRY(cudaGetLastError());
+    k2<<<(unsigned)(mt_bound * (H / gemm::kBN)), gemm::kThreads, smem, st>>>(g2);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
 }
 
 template <bool Q4, int BM>
@@ -717,7 +745,7 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     const int eoff = eng->cfg.expert_offset;
     gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk);
     gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
-                                                                                  w.mtile, gemm_tile_rows(eng, TK));
+                                                                                  w.mtile, std::abs(gemm_tile_rows(eng, TK)));
     gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk, w.starts, w.smap, w.tokmap);
     {
         const int nb = (int)(T * (H / 32));
@@ -744,8 +772,14 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     g2.sc_off = eng->rs2; g2.ss = eng->ss2; g2.nrec = H; g2.K = I; g2.N = H;
     g2.out = w.out;
     const int bm = gemm_tile_rows(eng, TK);
-    const int rc = bm == 16 ? launch_gemms<Q4, 16>(eng, g1, g2, TK, st)
-                            : (bm == 32 ? launch_gemms<Q4, 32>(eng, g1, g2, TK, st) : launch_gemms<Q4, 64>(eng, g1, g2, TK, st));
+    int rc;
+    switch (bm) {
+        case -8: rc = launch_gemms_wm<Q4, 8>(eng, g1, g2, TK, st); break;
+        case -16: rc = launch_gemms_wm<Q4, 16>(eng, g1, g2, TK, st); break;
+        case 16: rc = launch_gemms<Q4, 16>(eng, g1, g2, TK, st); break;
+        case 32: rc = launch_gemms<Q4, 32>(eng, g1, g2, TK, st); break;
+        default: rc = launch_gemms<Q4, 64>(eng, g1, g2, TK, st); break;
+    }
     if (rc) return rc;
     {
         const int64_t total = T * (H / 4);
@@ -786,9 +820,11 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (const char* v = std::getenv("MOE_GEMM_MIN_TOKENS")) eng->gemm_min_tokens = std::atoll(v);
     if (const char* v = std::getenv("MOE_DIST_REQUANT_MIN")) eng->dist_min_blocks = std::atoi(v);
     if (const char* v = std::getenv("MOE_DECODE_FLAGS")) eng->decode_flags = std::atoi(v);
-    if (const char* v = std::getenv("MOE_GEMM_BM")) {
-        const int bm = std::atoi(v);
-        eng->gemm_bm = (bm == 16 || bm == 32 || bm == 64) ? bm : 0;
+    if (const char* v = std::getenv("MOE_GEMM_BM")) {  // "w8" / "w16" weights-on-M, "16" / "32" / "64"
+        const bool wm = v[0] == 'w';
+        const int bm = std::atoi(wm ? v + 1 : v);
+        if (wm && (bm == 8 || bm == 16)) eng->gemm_bm = -bm;
+        else if (!wm && (bm == 16 || bm == 32 || bm == 64)) eng->gemm_bm = bm;
     }
     if (const char* v = std::getenv("MOE_DECODE_SK")) eng->use_sk = std::atoi(v) != 0;
     if (const char* v = std::getenv("MOE_SK_COST_A")) eng->sk_cost_a = std::max(0, std::atoi(v));

@@ -4,8 +4,8 @@
 //   route_count / route_scan / route_place  parallel stable counting sort of the
 //        T*K pairs by expert (moe_common.cpp:146-184): counts, starts, positions in
 //        (t,k) order, plus per-expert tile offsets for the GEMMs;
-//   quant_rows (gemm_kernels.cpp:25-58)     token rows -> Q8_0, in the weight's
-//        activation byte order;
+//   quant_rows (gemm_kernels.cpp:25-58)     token rows -> Q8_0, in the byte order that
+//        matches the weight's nibble order inside one MMA (act_elem);
 //   gemm_gate_up                            per (expert, 64-token tile, 64-unit tile):
 //        C = A x W^T over the expert's gathered token rows with int8 tensor-core
 //        MMAs, one MMA per 32-block and the reference's per-block fold
@@ -111,7 +111,16 @@ __global__ void route_place_kernel(const int32_t* ids, int TK, int E, int e_off,
     }
 }
 
-// Token rows -> Q8_0 (thread per 32-block), bytes in the weight format's order.
+// Byte order of a Q8_0 activation block on the GEMM path.  Q8_0: natural.  Q4_0
+// ("split" order): word w < 4 holds elements 8w+{0,2,4,6}, word 4+w holds 8w+{1,3,5,7},
+// so that MMA k positions 4w..4w+3 meet the low nibbles of weight word w and positions
+// 16+4w.. its high nibbles (weight word w = elements 8w..8w+7, nibble order).
+template <bool Q4>
+MOE_DEV int act_elem(int word, int byte) {
+    return Q4 ? (word < 4 ? 8 * word + 2 * byte : 8 * (word - 4) + 2 * byte + 1) : 4 * word + byte;
+}
+
+// Token rows -> Q8_0 (thread per 32-block), bytes in the GEMM path's order (act_elem).
 template <bool Q4>
 __global__ void quant_rows_kernel(const uint8_t* x, int act_bf16, int rows, int cols, int8_t* q, float* d,
                                   int32_t* s) {
@@ -146,10 +155,7 @@ __global__ void quant_rows_kernel(const uint8_t* x, int act_bf16, int rows, int 
         for (int k = 0; k < 8; ++k) {
             uint32_t w = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int e = Q4 ? 8 * (k >> 1) + (k & 1) + 2 * i : 4 * k + i;
-                w |= (uint32_t)(qv[e] & 0xff) << (8 * i);
-            }
+            for (int i = 0; i < 4; ++i) w |= (uint32_t)(qv[act_elem<Q4>(k, i)] & 0xff) << (8 * i);
             wv[k] = w;
         }
         uint4* dst = reinterpret_cast<uint4*>(q + (size_t)g * 32);
@@ -175,6 +181,25 @@ MOE_DEV void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2])
             "{%10,%11,%12,%13};"
             : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// D = A x B + C with A the weights (u8 nibbles for Q4_0, s8 for Q8_0) and B the s8 activations.
+template <bool AU8>
+MOE_DEV void mma_w(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], const int (&cin)[4]) {
+    if (AU8)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(cin[0]), "r"(cin[1]),
+              "r"(cin[2]), "r"(cin[3]));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(cin[0]), "r"(cin[1]),
+              "r"(cin[2]), "r"(cin[3]));
 }
 
 MOE_DEV void cp_async16(void* smem_dst, const void* gsrc, bool pred) {
@@ -357,10 +382,10 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
             for (int j = 0; j < NJ; ++j) {
                 const int n = wn * WC + j * 8 + g;
                 const uint32_t* wr = reinterpret_cast<const uint32_t*>(sB + n * S::kBRow + kb * (Q4 ? 16 : 32));
-                if (Q4) {
-                    const uint32_t w0 = wr[c >> 1], w1 = wr[2 + (c >> 1)];
-                    bf[j][0] = (c & 1) ? (w0 >> 4) & 0x0f0f0f0fu : w0 & 0x0f0f0f0fu;
-                    bf[j][1] = (c & 1) ? (w1 >> 4) & 0x0f0f0f0fu : w1 & 0x0f0f0f0fu;
+                if (Q4) {  // split activation order: k 4c.. = low nibbles of word c, 16+4c.. = high
+                    const uint32_t w0 = wr[c];
+                    bf[j][0] = w0 & 0x0f0f0f0fu;
+                    bf[j][1] = (w0 >> 4) & 0x0f0f0f0fu;
                 } else {
                     bf[j][0] = wr[c];
                     bf[j][1] = wr[4 + c];
@@ -445,10 +470,7 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
             for (int k = 0; k < 8; ++k) {
                 uint32_t w = 0;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int el = Q4 ? 8 * (k >> 1) + (k & 1) + 2 * q : 4 * k + q;
-                    w |= (uint32_t)(qv[el] & 0xff) << (8 * q);
-                }
+                for (int q = 0; q < 4; ++q) w |= (uint32_t)(qv[act_elem<Q4>(k, q)] & 0xff) << (8 * q);
                 wv[k] = w;
             }
             const int pos = pos0 + r;
@@ -477,6 +499,240 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
 }
 
 // y[t][n] = sum_k w[t,k] * out[smap[t,k]][n] in k order, cast.
+// ------------------------------------------------------------------ weights-on-M grouped GEMM
+// For few tokens per expert (<= 16): the weight rows are the MMA's M side (16 per warp,
+// 128 per CTA) and the tokens its N side (BT = 8 or 16 per tile), so an expert with 8
+// tokens fills every MMA column instead of half of a 16-token M tile.  Same per-block
+// fold, same outputs as grouped_gemm_kernel.  gate_up: warp w's m16 tile is gate rows
+// (rows 0-7) and up rows (rows 8-15) of the units u0+8w .. u0+8w+7, so one thread holds
+// the gate and up accumulators of the same (unit, token) and forms SiLU(gate)*up itself.
+template <bool Q4, int BT>
+struct StageW {
+    static constexpr int kWKB = kKB * (Q4 ? 16 : 32);  // weight bytes per row per stage
+    static constexpr int kWRow = kWKB + kRowPad;
+    static constexpr int kXKB = kKB * 32;               // activation bytes per token per stage
+    static constexpr int kXRow = kXKB + kRowPad;
+    static constexpr int kW = kBN * kWRow;
+    static constexpr int kX = BT * kXRow;
+    static constexpr int kWd = kBN * kKB * 2;
+    static constexpr int kXd = BT * kKB * 4;
+    static constexpr int kXs = BT * kKB * 4;
+    static constexpr int kBytes = kW + kX + kWd + kXd + kXs;
+};
+
+template <bool Q4, bool GATE_UP, int BT>
+__global__ void __launch_bounds__(kThreads) grouped_gemm_wm_kernel(const GemmParams p) {
+    using S = StageW<Q4, BT>;
+    constexpr int NJ = BT / 8;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, c = lane & 3;
+
+    // ---- tile -> (expert, token tile, weight-row tile)
+    const int ntiles_n = p.N / kBN;
+    const int mt_total = p.mtile_start[p.E];
+    const int tile = blockIdx.x;
+    if (tile >= mt_total * ntiles_n) return;
+    const int mt_glob = tile / ntiles_n, nt = tile % ntiles_n;
+    int lo = 0, hi = p.E;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (p.mtile_start[mid] <= mt_glob) lo = mid;
+        else hi = mid;
+    }
+    const int e = lo;
+    const int m0 = (mt_glob - p.mtile_start[e]) * BT;
+    const int cnt = p.counts[e];
+    const int pos0 = p.starts[e] + m0;
+    const int mtok = min(BT, cnt - m0);
+    const int nkb = p.K / 32;
+
+    __shared__ int64_t s_xrow[BT];
+    for (int r = tid; r < BT; r += kThreads) {
+        const int pos = pos0 + min(r, max(mtok, 1) - 1);
+        s_xrow[r] = GATE_UP ? (int64_t)(p.tokmap[pos] / p.topk) : (int64_t)pos;
+    }
+    __syncthreads();
+    const uint8_t* wexp = p.wbase + (int64_t)e * p.nrec * p.rec;
+    // smem weight row r (0..127) -> its quants / its scale field
+    auto w_row = [&](int r, int64_t& qoff, int64_t& soff) {
+        if (GATE_UP) {
+            const int w = r >> 4, rr = r & 15;
+            const int64_t unit = (int64_t)nt * (kBN / 2) + w * 8 + (rr & 7);
+            const int part = rr >> 3;  // 0 gate, 1 up
+            qoff = unit * p.rec + (int64_t)part * p.rs;
+            soff = unit * p.rec + p.sc_off + (int64_t)part * p.ss;
+        } else {
+            const int64_t row = (int64_t)nt * kBN + r;
+            qoff = row * p.rec;
+            soff = row * p.rec + p.sc_off;
+        }
+    };
+
+    auto load_stage = [&](int st, int kb0) {
+        uint8_t* base = smem + (size_t)st * S::kBytes;
+        uint8_t* sW = base;
+        int8_t* sX = reinterpret_cast<int8_t*>(base + S::kW);
+        uint16_t* sWd = reinterpret_cast<uint16_t*>(base + S::kW + S::kX);
+        float* sXd = reinterpret_cast<float*>(base + S::kW + S::kX + S::kWd);
+        int32_t* sXs = reinterpret_cast<int32_t*>(base + S::kW + S::kX + S::kWd + S::kXd);
+        for (int ch = tid; ch < kBN * (S::kWKB / 16); ch += kThreads) {
+            const int r = ch / (S::kWKB / 16), cc = ch % (S::kWKB / 16);
+            int64_t qo, so;
+            w_row(r, qo, so);
+            cp_async16(sW + r * S::kWRow + cc * 16, wexp + qo + (int64_t)kb0 * (Q4 ? 16 : 32) + cc * 16, true);
+        }
+        for (int ch = tid; ch < BT * (S::kXKB / 16); ch += kThreads) {
+            const int r = ch / (S::kXKB / 16), cc = ch % (S::kXKB / 16);
+            cp_async16(sX + r * S::kXRow + cc * 16, p.aq + s_xrow[r] * p.K + (int64_t)kb0 * 32 + cc * 16, r < mtok);
+        }
+        for (int r = tid; r < kBN; r += kThreads) {
+            int64_t qo, so;
+            w_row(r, qo, so);
+            const uint32_t d = smem_u32(sWd + r * kKB);
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(wexp + so + kb0 * 2) : "memory");
+        }
+        for (int r = tid; r < BT; r += kThreads) {
+            cp_async16(sXd + r * kKB, p.ad + s_xrow[r] * nkb + kb0, r < mtok);
+            if (Q4) cp_async16(sXs + r * kKB, p.as + s_xrow[r] * nkb + kb0, r < mtok);
+        }
+    };
+
+    float acc[NJ][4];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[j][q] = 0.f;
+
+    const int nsteps = (nkb + kKB - 1) / kKB;
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (s < nsteps) load_stage(s, s * kKB);
+        cp_async_commit();
+    }
+    const bool sbf = p.scale_bf16 != 0;
+    const int r0 = warp * 16 + g;  // this thread's weight rows r0, r0 + 8
+    for (int step = 0; step < nsteps; ++step) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();
+        {
+            const int nxt = step + kStages - 1;
+            if (nxt < nsteps) load_stage(nxt % kStages, nxt * kKB);
+            cp_async_commit();
+        }
+        const uint8_t* base = smem + (size_t)(step % kStages) * S::kBytes;
+        const uint8_t* sW = base;
+        const int8_t* sX = reinterpret_cast<const int8_t*>(base + S::kW);
+        const uint16_t* sWd = reinterpret_cast<const uint16_t*>(base + S::kW + S::kX);
+        const float* sXd = reinterpret_cast<const float*>(base + S::kW + S::kX + S::kWd);
+        const int32_t* sXs = reinterpret_cast<const int32_t*>(base + S::kW + S::kX + S::kWd + S::kXd);
+#pragma unroll 2
+        for (int kb = 0; kb < kKB; ++kb) {
+            uint32_t af[4];
+            {
+                const uint32_t* w0 = reinterpret_cast<const uint32_t*>(sW + r0 * S::kWRow + kb * (Q4 ? 16 : 32));
+                const uint32_t* w1 = reinterpret_cast<const uint32_t*>(sW + (r0 + 8) * S::kWRow + kb * (Q4 ? 16 : 32));
+                if (Q4) {  // word c: low nibbles -> k 4c.., high nibbles -> k 16+4c..
+                    const uint32_t x0 = w0[c], x1 = w1[c];
+                    af[0] = x0 & 0x0f0f0f0fu;
+                    af[1] = x1 & 0x0f0f0f0fu;
+                    af[2] = (x0 >> 4) & 0x0f0f0f0fu;
+                    af[3] = (x1 >> 4) & 0x0f0f0f0fu;
+                } else {
+                    af[0] = w0[c];
+                    af[1] = w1[c];
+                    af[2] = w0[4 + c];
+                    af[3] = w1[4 + c];
+                }
+            }
+            const float dw0 = scale_to_f32(sWd[r0 * kKB + kb], sbf), dw1 = scale_to_f32(sWd[(r0 + 8) * kKB + kb], sbf);
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                const int t0 = j * 8 + 2 * c;  // this thread's tokens t0, t0 + 1
+                const uint32_t* xr = reinterpret_cast<const uint32_t*>(sX + (j * 8 + g) * S::kXRow + kb * 32);
+                const uint32_t bf[2] = {xr[c], xr[4 + c]};
+                const float da0 = sXd[t0 * kKB + kb], da1 = sXd[(t0 + 1) * kKB + kb];
+                int cin[4] = {0, 0, 0, 0};
+                if (Q4) {  // remove the nibble bias: -8 * (sum of the token's block)
+                    const int s0 = -8 * sXs[t0 * kKB + kb], s1 = -8 * sXs[(t0 + 1) * kKB + kb];
+                    cin[0] = s0; cin[1] = s1; cin[2] = s0; cin[3] = s1;
+                }
+                int d[4];
+                mma_w<Q4>(d, af, bf, cin);
+                // d0: (row r0, token t0), d1: (r0, t0+1), d2: (r0+8, t0), d3: (r0+8, t0+1)
+                acc[j][0] += ((float)d[0] * dw0) * da0;
+                acc[j][1] += ((float)d[1] * dw0) * da1;
+                acc[j][2] += ((float)d[2] * dw1) * da0;
+                acc[j][3] += ((float)d[3] * dw1) * da1;
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    if (GATE_UP) {
+        // h[token][unit] = SiLU(gate) * up, staged [BT][kBN/2 + 1] fp32, then requantised per
+        // (token, 32-unit block)
+        float* hsm = reinterpret_cast<float*>(smem);
+        constexpr int HW = kBN / 2 + 1;
+        const int ul = warp * 8 + g;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const int t0 = j * 8 + 2 * c;
+            hsm[t0 * HW + ul] = silu_mul(acc[j][0], acc[j][2]);
+            hsm[(t0 + 1) * HW + ul] = silu_mul(acc[j][1], acc[j][3]);
+        }
+        __syncthreads();
+        const int I = p.N / 2, nbI = I / 32;
+        const int u0 = nt * (kBN / 2);
+        for (int t = tid; t < BT * (kBN / 64); t += kThreads) {
+            const int r = t / (kBN / 64), blk = t % (kBN / 64);
+            if (r >= mtok) continue;
+            float v[32];
+            float amax = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                v[k] = hsm[r * HW + blk * 32 + k];
+                amax = fmaxf(amax, fabsf(v[k]));
+            }
+            const float dd = q8_scale(amax);
+            const float id = q8_inv(dd);
+            int qv[32];
+            int sum = 0;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                qv[k] = q8_quant(v[k], id);
+                sum += qv[k];
+            }
+            uint32_t wv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                uint32_t w = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) w |= (uint32_t)(qv[act_elem<Q4>(k, q)] & 0xff) << (8 * q);
+                wv[k] = w;
+            }
+            const int pos = pos0 + r;
+            const int b = u0 / 32 + blk;
+            uint4* dst = reinterpret_cast<uint4*>(p.hq + (int64_t)pos * I + b * 32);
+            dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            p.hd[(int64_t)pos * nbI + b] = dd;
+            if (Q4) p.hs[(int64_t)pos * nbI + b] = sum;
+        }
+    } else {
+        const int n0 = nt * kBN;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int t = j * 8 + 2 * c + (q & 1);
+                if (t >= mtok) continue;
+                const int row = n0 + r0 + (q >> 1) * 8;
+                p.out[(int64_t)(pos0 + t) * p.N + row] = acc[j][q];
+            }
+    }
+}
+
 __global__ void combine_kernel(const float* out, const int32_t* smap, const float* tw, int T, int K, int H,
                                void* y, int out_kind) {
     const int64_t total = (int64_t)T * (H / 4);
