@@ -368,10 +368,22 @@ def run_ours(args):
         nbytes.append(int(torch.unique(ids).numel()) * bpe)
     combine_out = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(nin)]
 
+    # N>1, decode sizes: the partials are summed inside the fused kernel over NVLink peer
+    # memory (every rank maps every other rank's mailbox); larger T: fp32 partial + NCCL.
+    fused = world > 1 and not args.nccl_combine and handles[0].p2p_covers(T)
+    if fused:
+        for h in handles:
+            hnd = h.p2p_mailbox(world, max(T, 8)).to(dev)
+            allh = [torch.empty_like(hnd) for _ in range(world)]
+            dist.all_gather(allh, hnd)
+            h.p2p_connect(torch.stack(allh).cpu())
+        torch.cuda.synchronize()
+        dist.barrier()
+
     def step(i):
         h = handles[i % nsets]
         j = i % nin
-        if world == 1:
+        if world == 1 or fused:
             return torch.ops.nanovllm.moe_forward(xs[j], idss[j], wss[j], h)
         part = torch.ops.nanovllm.moe_forward_partial(xs[j], idss[j], wss[j], h)
         dist.all_reduce(part)
@@ -383,7 +395,7 @@ def run_ours(args):
     graphs = None
     cycle_graph = None
     ncycle = int(np.lcm(nsets, nin))
-    if world == 1 and not args.no_graph:  # N>1: eager launches + NCCL (its capture is not used)
+    if (world == 1 or fused) and not args.no_graph:  # NCCL steps are not captured
         try:
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
@@ -475,17 +487,21 @@ def run_ours(args):
                       "l2": f"inputs larger than L2: {nsets} rotating weight sets x {E} experts "
                             f"({nsets * E * bpe / 1e9:.1f} GB) and {nin} rotating routings",
                       "parallelism": f"ep{world}" if world > 1 else "single",
+                      "combine": ("in-kernel over NVLink peer memory" if fused else "fp32 partial + NCCL all-reduce")
+                      if world > 1 else "in-kernel",
                       "launch": (f"cuda_graph ({ncycle} layer steps per graph replay)" if cycle_graph is not None
                                  else "eager"),
                       "avg_active_experts": round(avg_bytes / bpe, 2)},
-           "gpu_launches": args.steps * (1 if world == 1 else 1),
+           "gpu_launches": args.steps * (1 if T <= 8 or args.quant == "awq" else 7),
            "clocks": clocks}
     if True:
         out["roofline"] = {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
                            "frac": round(value / peak, 4), "peak_source": peak_kind,
                            "traffic": NCU_TRAFFIC_BYTES,
                            "algorithmic_bytes_per_launch": round(avg_bytes),
-                           "kernel": "moe_decode_kernel" if T <= 32 or args.quant == "awq" else "grouped_gemm_kernel"}
+                           "kernel": ("moe_decode_kernel" if T == 1 or args.quant == "awq" else
+                                      "moe_decode_sk_kernel" if T <= 8 else
+                                      "grouped_gemm_wm_kernel" if T * K <= 24 * E else "grouped_gemm_kernel")}
     # end-to-end through the public op with host buffers and copies in the timed region
     if rank == 0 or world > 1:
         xh = [x.cpu().pin_memory() for x in xs]
@@ -594,6 +610,7 @@ def main():
     ap.add_argument("--routing", default="softmax", choices=["softmax", "zipf"])
     ap.add_argument("--sweep-tokens", default="1,4,8,32,128,1024,4096")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock soak (profiling runs)")
+    ap.add_argument("--nccl-combine", action="store_true", help="N>1: fp32 partial + NCCL all-reduce at every T")
     ap.add_argument("--cpu-worker", type=float, default=None)
     args = ap.parse_args()
     if args.cpu_worker is not None:

@@ -158,6 +158,25 @@ int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* y, const in
 /* Message of the last failed call on this thread ("" if none). */
 const char* moe_last_error(void);
 
+/* Expert-parallel combine over peer memory (no counterpart in the reference, whose NUMA
+ * "TP" nodes reduce into node 0, q8_gemm.cpp:621-641).  One process per GPU; rank r's
+ * engine holds experts [r*E/W, (r+1)*E/W) (moe_config.expert_offset).  Each rank creates a
+ * mailbox for `world` ranks and up to min(max_tokens, 64) tokens per decode launch and gets
+ * its CUDA IPC handle (64 bytes) back; the caller exchanges the handles (e.g. an all-gather)
+ * and passes all of them, in rank order, to moe_engine_p2p_connect.  From then on,
+ * moe_engine_forward calls that take the fused decode kernels sum the ranks' partials
+ * inside the kernel (NVLink stores into every rank's mailbox, per-CTA flags, bounded
+ * waits) and write the full output on every rank; all ranks must make the same sequence
+ * of such calls.  While connected, calls that moe_engine_p2p_covers() rejects (the
+ * grouped-GEMM sizes) fail with MOE_ERR_STATE: disable the combine with
+ * moe_engine_p2p_enable(eng, 0), run the layer with MOE_F32 output (this rank's partial) and
+ * all-reduce it, then enable it again.  A peer that does not arrive within about a second
+ * sets device error 4 (moe_engine_device_error). */
+int moe_engine_p2p_mailbox(moe_engine* eng, int32_t world, int64_t max_tokens, void* ipc_handle_out);
+int moe_engine_p2p_connect(moe_engine* eng, int32_t rank, int32_t world, const void* ipc_handles);
+int moe_engine_p2p_enable(moe_engine* eng, int32_t on);
+int moe_engine_p2p_covers(moe_engine* eng, int64_t num_tokens);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,12 @@ struct moe_engine {
     bool use_sk = true;  // decode through moe_decode_sk_kernel when the layout allows
     int32_t sk_cost_a = 3;  // its chunk cost model: streaming share per chunk vs one token of compute
     int32_t sk_min_chunks_per_cta = 2;  // use it from this many (unique expert x I/32) chunks per CTA
+    // expert-parallel combine over peer memory (moe_engine_p2p_mailbox / _connect)
+    uint8_t* mbox = nullptr;   // this rank's mailbox: data [2][world][tcap][H] fp32 | flags [world][num_sms] u64
+    int64_t mbox_data_bytes = 0;
+    int p2p_world = 1, p2p_rank = 0, p2p_tcap = 0;
+    bool p2p_active = false;  // connected and enabled: decode launches sum over the ranks
+    void* peer_base[kMaxPeers] = {};  // opened peer mailboxes (nullptr for this rank)
     float* part = nullptr;  // per-CTA fp32 partial tiles [num_sms][part_cap][H] of the split-K kernel
     int64_t part_cap = 0;
     // workspace
@@ -850,6 +856,9 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     cudaFree(eng->dn);
     cudaFree(eng->dk);
     cudaFree(eng->part);
+    for (int q = 0; q < kMaxPeers; ++q)
+        if (eng->peer_base[q]) cudaIpcCloseMemHandle(eng->peer_base[q]);
+    cudaFree(eng->mbox);
     cudaFree(eng->h_ws);
     cudaFree(eng->bar);
     cudaFree(eng->timeline);
@@ -996,6 +1005,21 @@ extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t t
     return ensure_workspace(eng, std::min<int64_t>(max_tokens, 64) * top_k);
 }
 
+extern "C" int moe_engine_p2p_covers(moe_engine* eng, int64_t num_tokens);
+
+// Peer-combine parameters of a decode launch.
+void fill_peer_combine(moe_engine* eng, PeerCombine& pc) {
+    std::memset(&pc, 0, sizeof(pc));
+    pc.rank = eng->p2p_rank;
+    pc.world = eng->p2p_world;
+    pc.tcap = eng->p2p_tcap;
+    for (int q = 0; q < eng->p2p_world; ++q) {
+        uint8_t* base = q == eng->p2p_rank ? eng->mbox : static_cast<uint8_t*>(eng->peer_base[q]);
+        pc.data[q] = reinterpret_cast<float*>(base);
+        pc.flag[q] = reinterpret_cast<unsigned long long*>(base + eng->mbox_data_bytes);
+    }
+}
+
 extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const int32_t* topk_ids,
                                   const float* topk_w, int64_t T, int64_t K, int32_t act_dtype, int32_t out_dtype,
                                   void* stream) {
@@ -1011,6 +1035,8 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     if (T == 0) return MOE_OK;
     const int64_t H = eng->cfg.hidden_size;
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
+    if (eng->p2p_active && !moe_engine_p2p_covers(eng, T))
+        return fail(MOE_ERR_STATE, "peer combine covers decode-size calls only; use the fp32 partial and an all-reduce");
     if (T > eng->gemm_min_tokens && gemm_path_ok(eng)) {  // dense enough for the grouped GEMMs
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
         CUDA_TRY(cudaStreamIsCapturing(st, &cap));
@@ -1060,6 +1086,10 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         p.gu = eng->gu; p.dn = eng->dn;
         p.h_ws = eng->h_ws; p.bar = reinterpret_cast<unsigned long long*>(eng->bar); p.err = eng->err;
         p.dk = eng->dk; p.part = eng->part;
+        if (eng->p2p_active) {
+            if (n > eng->p2p_tcap) return fail(MOE_ERR_INVALID, "tokens per decode launch exceed the mailbox capacity");
+            fill_peer_combine(eng, p.pc);
+        }
         p.dbg = eng->timeline;
         const int qt = eng->cfg.quant_type;
         const int rc = qt == MOE_Q4_0 ? launch_decode<kQ4>(pl, st)
@@ -1245,6 +1275,7 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
     if (out_dtype != MOE_F16 && out_dtype != MOE_BF16 && out_dtype != MOE_F32)
         return fail(MOE_ERR_INVALID, "bad output dtype");
     if (T > 0 && (!x || !y || !topk_ids || !topk_w)) return fail(MOE_ERR_INVALID, "null tensor pointer");
+    if (eng->p2p_active) return fail(MOE_ERR_STATE, "the no-allocation forward does not run the peer combine");
     const int64_t I = eng->cfg.intermediate_size;
     const int64_t P = T * K;
     const size_t need = kNoAllocHeader + (size_t)8 * P * (I / 32) + (size_t)P * I * 4;
@@ -1279,4 +1310,57 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
     const int qt = eng->cfg.quant_type;
     return qt == MOE_Q4_0 ? launch_decode<kQ4>(pl, st)
                           : (qt == MOE_AWQ ? launch_decode<kAWQ>(pl, st) : launch_decode<kQ8>(pl, st));
+}
+
+// =================================================================== peer combine (expert parallel)
+extern "C" int moe_engine_p2p_covers(moe_engine* eng, int64_t num_tokens) {
+    if (!eng) return 0;
+    return !(num_tokens > eng->gemm_min_tokens && gemm_path_ok(eng)) && num_tokens <= std::max<int64_t>(eng->p2p_tcap, 8);
+}
+
+extern "C" int moe_engine_p2p_mailbox(moe_engine* eng, int32_t world, int64_t max_tokens, void* ipc_handle_out) {
+    if (int rc = check_engine(eng)) return rc;
+    if (world < 2 || world > kMaxPeers || max_tokens <= 0 || !ipc_handle_out)
+        return fail(MOE_ERR_INVALID, "peer combine needs 2..8 ranks, max_tokens > 0 and a handle buffer");
+    if (eng->mbox) return fail(MOE_ERR_STATE, "mailbox already created");
+    DeviceGuard g(eng->cfg.device);
+    const int64_t tcap = std::min<int64_t>(max_tokens, 64);
+    const size_t data = (size_t)2 * world * tcap * eng->cfg.hidden_size * sizeof(float);
+    const size_t flags = (size_t)world * eng->num_sms * sizeof(unsigned long long);
+    CUDA_TRY(cudaMalloc(&eng->mbox, data + flags));
+    CUDA_TRY(cudaMemset(eng->mbox, 0, data + flags));
+    eng->mbox_data_bytes = (int64_t)data;
+    eng->p2p_tcap = (int)tcap;
+    cudaIpcMemHandle_t h;
+    CUDA_TRY(cudaIpcGetMemHandle(&h, eng->mbox));
+    std::memcpy(ipc_handle_out, &h, sizeof(h));
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_p2p_connect(moe_engine* eng, int32_t rank, int32_t world, const void* ipc_handles) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!eng->mbox) return fail(MOE_ERR_STATE, "create the mailbox first (moe_engine_p2p_mailbox)");
+    if (world < 2 || world > kMaxPeers || rank < 0 || rank >= world || !ipc_handles)
+        return fail(MOE_ERR_INVALID, "bad rank / world / handles");
+    if (eng->mbox_data_bytes != (int64_t)2 * world * eng->p2p_tcap * eng->cfg.hidden_size * (int64_t)sizeof(float))
+        return fail(MOE_ERR_INVALID, "world differs from the mailbox's");
+    DeviceGuard g(eng->cfg.device);
+    const auto* hs = static_cast<const cudaIpcMemHandle_t*>(ipc_handles);
+    for (int q = 0; q < world; ++q) {
+        if (q == rank) continue;
+        void* ptr = nullptr;
+        CUDA_TRY(cudaIpcOpenMemHandle(&ptr, hs[q], cudaIpcMemLazyEnablePeerAccess));
+        eng->peer_base[q] = ptr;
+    }
+    eng->p2p_rank = rank;
+    eng->p2p_world = world;
+    eng->p2p_active = true;
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_p2p_enable(moe_engine* eng, int32_t on) {
+    if (int rc = check_engine(eng)) return rc;
+    if (on && eng->p2p_world < 2) return fail(MOE_ERR_STATE, "not connected (moe_engine_p2p_connect)");
+    eng->p2p_active = on != 0;
+    return MOE_OK;
 }

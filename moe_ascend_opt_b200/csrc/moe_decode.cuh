@@ -39,6 +39,21 @@ enum Fmt : int { kQ8 = 0, kQ4 = 1, kAWQ = 2 };
 //   has arrived, so the gate_up bytes (on the critical path) are not queued behind them.
 constexpr int kFlagEvictFirst = 1, kFlagLateDown = 2;
 
+// Expert-parallel combine over peer memory (one process per GPU, NVLink P2P).  Every
+// rank owns a mailbox [2 parities][world sources][tcap tokens][H] fp32 followed by flags
+// [world sources][grid] u64; `data[q]` / `flag[q]` point into rank q's mailbox (this
+// process's mapping of it).  CTA c of every rank covers the same output rows, so the
+// exchange is CTA-to-CTA: no grid-wide step.
+constexpr int kMaxPeers = 8;
+struct PeerCombine {
+    float* data[kMaxPeers];
+    unsigned long long* flag[kMaxPeers];
+    int32_t rank, world, tcap;
+};
+// The exchange epoch of a launch is its index on the engine's launch counter plus one
+// (read by every CTA at the start, so graph replays get fresh epochs); ranks that make the
+// same sequence of calls count the same epochs.
+
 struct DecodeParams {
     // gate_up unit records [E][I]: gate qs row j (rs1) | up qs row j (rs1) | gate scales (ss1) | up scales (ss1)
     const uint8_t* gu;
@@ -66,7 +81,64 @@ struct DecodeParams {
     int32_t flags;            // kFlagEvictFirst | kFlagLateDown
     int32_t sk_cost_a;        // split-K kernel: cost of streaming one chunk, in units of one token's compute
     unsigned long long* dbg;  // optional per-CTA phase stamps [grid][kStamps] (globaltimer ns)
+    PeerCombine pc;           // pc.world > 1: the output rows are summed over the ranks' partials
 };
+
+MOE_DEV void st_out(const DecodeParams& p, size_t o, float v) {
+    if (p.out_kind == 2) reinterpret_cast<float*>(p.y)[o] = v;
+    else if (p.out_kind == 1) reinterpret_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(v);
+    else reinterpret_cast<__half*>(p.y)[o] = __float2half_rn(v);
+}
+
+// This rank's partial of output element (t, n) into slot [parity][rank] of every rank's mailbox.
+MOE_DEV void pc_put(const DecodeParams& p, unsigned long long epoch, int t, int n, float v) {
+    const PeerCombine& pc = p.pc;
+    const size_t o = (((size_t)(epoch & 1) * pc.world + pc.rank) * pc.tcap + t) * p.H + n;
+    for (int q = 0; q < pc.world; ++q) pc.data[q][o] = v;
+}
+
+// After every thread of the CTA has put its rows [n0, n0+R): publish this CTA's flag on
+// every rank, wait (bounded) for CTA `cta` of every other rank, then sum the partials in
+// rank order (deterministic) and write the output rows.  Returns false when a peer did not
+// arrive within the wait budget (the error word is set; the rows are left unwritten).
+MOE_DEV bool pc_finish(const DecodeParams& p, unsigned long long epoch, int cta, int G, int n0, int R, int tid) {
+    const PeerCombine& pc = p.pc;
+    __shared__ int s_pc_ok;
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");  // this CTA's puts before its flags
+        for (int q = 0; q < pc.world; ++q)
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(pc.flag[q] + (size_t)pc.rank * G + cta),
+                         "l"(epoch)
+                         : "memory");
+        int ok = 1;
+        for (int src = 0; src < pc.world && ok; ++src) {
+            if (src == pc.rank) continue;
+            const unsigned long long* f = pc.flag[pc.rank] + (size_t)src * G + cta;
+            uint32_t it = 0;
+            for (;; ++it) {
+                unsigned long long v;
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+                if (v >= epoch) break;
+                if (it >= kSpinLimit) { ok = 0; break; }
+                if (it > 256) __nanosleep(256);
+            }
+        }
+        if (!ok) atomicExch(p.err, kErrPeerWait);
+        s_pc_ok = ok;
+    }
+    __syncthreads();
+    if (!s_pc_ok) return false;
+    const float* mine = pc.data[pc.rank];
+    const size_t par = (size_t)(epoch & 1) * pc.world;
+    for (int idx = tid; idx < p.T * R; idx += blockDim.x) {
+        const int t = idx / R, n = n0 + idx % R;
+        float acc = 0.f;
+        for (int src = 0; src < pc.world; ++src) acc += __ldcv(mine + ((par + src) * pc.tcap + t) * p.H + n);
+        st_out(p, (size_t)t * p.H + n, acc);
+    }
+    return true;
+}
 
 MOE_DEV unsigned long long global_ns() {
     unsigned long long t;
@@ -820,11 +892,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
             if (pos < 0) continue;
             acc += p.tw[t * p.K + k] * outs[(size_t)pos * p.rows_max + r];
         }
-        const size_t o = (size_t)t * H + n0 + r;
-        if (p.out_kind == 2) reinterpret_cast<float*>(p.y)[o] = acc;
-        else if (p.out_kind == 1) reinterpret_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(acc);
-        else reinterpret_cast<__half*>(p.y)[o] = __float2half_rn(acc);
+        if (p.pc.world > 1) pc_put(p, launch + 1, t, n0 + r, acc);
+        else st_out(p, (size_t)t * H + n0 + r, acc);
     }
+    if (p.pc.world > 1) pc_finish(p, launch + 1, cta, G, n0, R, tid);
     if (dbg && tid == 0) { dbg[12] = global_ns(); dbg[14] = clock64(); }
 }
 

@@ -378,11 +378,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_sk_kernel(const Decode
         float acc = 0.f;
         for (int g = 0; g < ks; ++g) acc += gsum[g * O + o];
         const int t = o / R, r = o - t * R;
-        const size_t oi = (size_t)t * H + n0 + r;
-        if (p.out_kind == 2) reinterpret_cast<float*>(p.y)[oi] = acc;
-        else if (p.out_kind == 1) reinterpret_cast<__nv_bfloat16*>(p.y)[oi] = __float2bfloat16_rn(acc);
-        else reinterpret_cast<__half*>(p.y)[oi] = __float2half_rn(acc);
+        if (p.pc.world > 1) pc_put(p, s_launch + 1, t, n0 + r, acc);
+        else st_out(p, (size_t)t * H + n0 + r, acc);
     }
+    if (p.pc.world > 1) pc_finish(p, s_launch + 1, cta, G, n0, R, tid);
     if (dbg && tid == 0) { dbg[9] = global_ns(); dbg[14] = clock64(); }
 }
 

@@ -8,6 +8,7 @@
 //     .get_last_run_time_ms() / get_quant_type() / get_num_experts() /
 //      get_hidden_size() / get_intermediate_size()              :372-391
 //     new: store_awq(...), set_expert_parallel(rank, size), set_group_size(g),
+//          p2p_mailbox / p2p_connect / p2p_covers / p2p_enable (peer-memory combine),
 //          reserve(T, K), export_expert(e, which), device_error()
 //   torch.ops.nanovllm.moe_forward(hidden, topk_ids, topk_w, moe)          :402
 //   torch.ops.nanovllm.moe_forward_npu_stream(...)   same schema, CUDA stream :405
@@ -203,6 +204,28 @@ struct MoEInferHandle : torch::CustomClassHolder {
                  "moe_forward");
     }
 
+    // expert-parallel combine over peer memory (include/moe_b200.h, moe_engine_p2p_*)
+    at::Tensor p2p_mailbox(int64_t world, int64_t max_tokens) {
+        TORCH_CHECK(eng, "no weights loaded");
+        TORCH_CHECK(world == ep_size, "world must equal the expert-parallel size");
+        c10::cuda::CUDAGuard g(device);
+        auto h = at::zeros({64}, at::TensorOptions().dtype(at::kByte));
+        check_rc(moe_engine_p2p_mailbox(eng, (int32_t)world, max_tokens, h.data_ptr()), "p2p_mailbox");
+        return h;
+    }
+    void p2p_connect(const at::Tensor& handles) {
+        TORCH_CHECK(eng, "no weights loaded");
+        auto h = handles.to(at::kCPU).contiguous();
+        TORCH_CHECK(h.scalar_type() == at::kByte && h.numel() == ep_size * 64, "handles must be uint8 [world, 64]");
+        c10::cuda::CUDAGuard g(device);
+        check_rc(moe_engine_p2p_connect(eng, (int32_t)ep_rank, (int32_t)ep_size, h.data_ptr()), "p2p_connect");
+    }
+    bool p2p_covers(int64_t T) { return eng && moe_engine_p2p_covers(eng, T); }
+    void p2p_enable(bool on) {
+        TORCH_CHECK(eng, "no weights loaded");
+        check_rc(moe_engine_p2p_enable(eng, on ? 1 : 0), "p2p_enable");
+    }
+
     double last_ms() {
         if (!eng) return 0.0;
         double ms = 0.0;
@@ -297,6 +320,10 @@ TORCH_LIBRARY(nanovllm, m) {
         .def("store_awq", &MoEInferHandle::store_awq)
         .def("set_expert_parallel", &MoEInferHandle::set_expert_parallel)
         .def("set_group_size", &MoEInferHandle::set_group_size)
+        .def("p2p_mailbox", &MoEInferHandle::p2p_mailbox)
+        .def("p2p_connect", &MoEInferHandle::p2p_connect)
+        .def("p2p_covers", &MoEInferHandle::p2p_covers)
+        .def("p2p_enable", &MoEInferHandle::p2p_enable)
         .def("get_last_run_time_ms", [](const c10::intrusive_ptr<MoEInferHandle>& s) { return s->last_ms(); })
         .def("get_quant_type",
              [](const c10::intrusive_ptr<MoEInferHandle>& s) -> std::string {

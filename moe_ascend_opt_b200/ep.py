@@ -7,6 +7,9 @@ the fused layer over its local experts only -- ids outside the block are
 skipped exactly like invalid ids in the reference (moe_common.cpp:158,175-181)
 -- and produces an fp32 partial sum; one all-reduce over NCCL (NVLink /
 NVSwitch) adds the partials, then the result is cast to the hidden dtype.
+After `connect_peers()`, decode-size calls instead sum the partials inside the fused
+kernel: each CTA stores its output rows into every rank's mailbox over NVLink and waits
+(bounded) for the same CTA of the other ranks.
 This replaces the reference's NUMA "TP" split (moe_infer.cpp:143-205,
 q8_gemm.cpp:621-641), whose node-0 reduction becomes the all-reduce.
 """
@@ -63,14 +66,43 @@ class ExpertParallelMoE:
     def quantize_and_store_expert(self, e: int, proj: str, w):
         self.handle.quantize_and_store_expert(e, proj, w)
 
-    def forward(self, hidden, topk_ids, topk_w, out: Optional[object] = None):
+    def connect_peers(self, max_tokens: int = 8) -> None:
+        """Set up the in-kernel combine over peer memory (NVLink): every rank creates its
+        mailbox, the CUDA IPC handles are all-gathered over the process group, and each
+        rank maps the others'.  Afterwards decode-size forwards sum the ranks' partials
+        inside the fused kernel; larger ones still use the partial + all-reduce path."""
         import torch
         import torch.distributed as dist
 
         if self.world == 1:
+            return
+        h = self.handle.p2p_mailbox(self.world, max_tokens)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        mine = h.to(dev)
+        allh = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(allh, mine, group=self.group)
+        self.handle.p2p_connect(torch.stack(allh).cpu())
+        self.peers = True
+
+    peers = False
+
+    def forward(self, hidden, topk_ids, topk_w, out: Optional[object] = None):
+        import torch
+        import torch.distributed as dist
+
+        T = hidden.shape[0]
+        if self.world == 1:
             y = torch.ops.nanovllm.moe_forward(hidden, topk_ids, topk_w, self.handle)
+        elif self.peers and self.handle.p2p_covers(T):
+            y = torch.ops.nanovllm.moe_forward(hidden, topk_ids, topk_w, self.handle)  # summed in the kernel
         else:
-            part = torch.ops.nanovllm.moe_forward_partial(hidden, topk_ids, topk_w, self.handle)
+            if self.peers:
+                self.handle.p2p_enable(False)
+            try:
+                part = torch.ops.nanovllm.moe_forward_partial(hidden, topk_ids, topk_w, self.handle)
+            finally:
+                if self.peers:
+                    self.handle.p2p_enable(True)
             dist.all_reduce(part, group=self.group)
             y = part.to(hidden.dtype)
         if out is not None:
