@@ -469,6 +469,7 @@ def run_ours(args):
             timed(min(args.steps, 2000))
         total_ms = timed(args.steps)
     clocks = clk.summary()
+    dev_errors = sorted({int(h.device_error()) for h in handles} - {0})
 
     avg_bytes = sum(nbytes[i % nin] for i in range(args.steps)) / args.steps
     qname = {"q4": "Q4_0", "q8": "Q8_0", "awq": "AWQ W4A16 g128"}[args.quant]
@@ -494,6 +495,8 @@ def run_ours(args):
                       "avg_active_experts": round(avg_bytes / bpe, 2)},
            "gpu_launches": args.steps * (1 if T <= 8 or args.quant == "awq" else 7),
            "clocks": clocks}
+    if dev_errors:
+        out["device_errors"] = dev_errors
     if True:
         out["roofline"] = {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
                            "frac": round(value / peak, 4), "peak_source": peak_kind,

@@ -28,10 +28,12 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, outdir, qt, E, H, I, K):
+def _worker(rank, world, port, outdir, qt, E, H, I, K, sk_min):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    if sk_min is not None:
+        os.environ["MOE_SK_MIN_CHUNKS"] = sk_min  # read when the engine is created
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     import moe_ascend_opt_b200  # noqa: F401
@@ -56,15 +58,16 @@ def _worker(rank, world, port, outdir, qt, E, H, I, K):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("sk_min", [None, "0"])  # default kernel choice / split-K kernel at every T
 @pytest.mark.parametrize("qt", [1])
-def test_two_rank_peer_combine_matches_oracle(qt):
+def test_two_rank_peer_combine_matches_oracle(qt, sk_min):
     import torch.multiprocessing as mp
 
     from oracle import oracle as O
 
     E, H, I, K = 32, 1024, 384, 8
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(2, _free_port(), d, qt, E, H, I, K), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, _free_port(), d, qt, E, H, I, K, sk_min), nprocs=2, join=True)
         gq, gd, dq, dd = q_weights(qt, E, H, I, 5)
         for T, seed in CASES:
             _, xf, ids, w = tokens(T, H, E, K, seed)
