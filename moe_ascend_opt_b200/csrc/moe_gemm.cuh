@@ -183,6 +183,25 @@ MOE_DEV void mma_s8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// D = A x B + C with A the s8 activations and B the weights (u8 nibbles for Q4_0, s8 for Q8_0).
+template <bool BU8>
+MOE_DEV void mma_a8(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], const int (&cin)[4]) {
+    if (BU8)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(cin[0]), "r"(cin[1]),
+              "r"(cin[2]), "r"(cin[3]));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%10,%11,%12,%13};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(cin[0]), "r"(cin[1]),
+              "r"(cin[2]), "r"(cin[3]));
+}
+
 // D = A x B + C with A the weights (u8 nibbles for Q4_0, s8 for Q8_0) and B the s8 activations.
 template <bool AU8>
 MOE_DEV void mma_w(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], const int (&cin)[4]) {
@@ -201,6 +220,18 @@ MOE_DEV void mma_w(int (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2], 
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "r"(cin[0]), "r"(cin[1]),
               "r"(cin[2]), "r"(cin[3]));
 }
+
+// Four 8x8 b16 matrices from shared memory (lane l gives the address of row l&7 of matrix l>>3).
+MOE_DEV void ldsm_x4(uint32_t (&r)[4], const void* row) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(row)));
+}
+MOE_DEV void ldsm_x2(uint32_t (&r)[2], const void* row) {  // lanes 0-15 give the row addresses
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(row)));
+}
+MOE_DEV float f4_get(const float4& v, int i) { return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w)); }
+MOE_DEV int i4_get(const int4& v, int i) { return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w)); }
 
 MOE_DEV void cp_async16(void* smem_dst, const void* gsrc, bool pred) {
     const uint32_t d = smem_u32(smem_dst);
@@ -364,63 +395,72 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_kernel(const GemmParams
         const float* sAd = reinterpret_cast<const float*>(base + S::kA + S::kB);
         const int32_t* sAs = reinterpret_cast<const int32_t*>(base + S::kA + S::kB + S::kAd);
         const uint16_t* sBd = reinterpret_cast<const uint16_t*>(base + S::kA + S::kB + S::kAd + S::kAs);
-#pragma unroll 2
+        // raw weight scales of the thread's columns for the stage's 4 blocks (8 B each)
+        uint2 dwr[NJ][2];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) dwr[j][h] = *reinterpret_cast<const uint2*>(sBd + (wn * WC + j * 8 + 2 * c + h) * kKB);
+        const int lm = lane >> 3, lr = lane & 7;  // ldmatrix: lane gives row lr of matrix lm
         for (int kb = 0; kb < kKB; ++kb) {
-            uint32_t af[MI][4];
-#pragma unroll
-            for (int i = 0; i < MI; ++i) {
-                const int r = wm * WR + i * 16 + g;
-                const uint32_t* ra = reinterpret_cast<const uint32_t*>(sA + r * S::kARow + kb * 32);
-                const uint32_t* rb = reinterpret_cast<const uint32_t*>(sA + (r + 8) * S::kARow + kb * 32);
-                af[i][0] = ra[c];
-                af[i][1] = rb[c];
-                af[i][2] = ra[4 + c];
-                af[i][3] = rb[4 + c];
-            }
             uint32_t bf[NJ][2];
+            if (Q4 && NJ == 4) {  // matrices = n8 tiles 0..3 of block kb (16 B rows)
+                uint32_t x[4];
+                ldsm_x4(x, sB + (wn * WC + lm * 8 + lr) * S::kBRow + kb * 16);
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) {
-                const int n = wn * WC + j * 8 + g;
-                const uint32_t* wr = reinterpret_cast<const uint32_t*>(sB + n * S::kBRow + kb * (Q4 ? 16 : 32));
-                if (Q4) {  // split activation order: k 4c.. = low nibbles of word c, 16+4c.. = high
-                    const uint32_t w0 = wr[c];
-                    bf[j][0] = w0 & 0x0f0f0f0fu;
-                    bf[j][1] = (w0 >> 4) & 0x0f0f0f0fu;
-                } else {
-                    bf[j][0] = wr[c];
-                    bf[j][1] = wr[4 + c];
+                for (int j = 0; j < 4; ++j) {  // split activation order: low nibbles k 4c.., high 16+4c..
+                    bf[j][0] = x[j] & 0x0f0f0f0fu;
+                    bf[j][1] = (x[j] >> 4) & 0x0f0f0f0fu;
+                }
+            } else if (Q4) {  // NJ == 2: matrices (tile 0, kb), (tile 1, kb), rows 16 B; x2
+                uint32_t x[2];
+                ldsm_x2(x, sB + (wn * WC + (lm & 1) * 8 + lr) * S::kBRow + kb * 16);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    bf[j][0] = x[j] & 0x0f0f0f0fu;
+                    bf[j][1] = (x[j] >> 4) & 0x0f0f0f0fu;
+                }
+            } else {  // (tile j0, bytes 0-15), (j0, 16-31), (j0+1, 0-15), (j0+1, 16-31)
+#pragma unroll
+                for (int j0 = 0; j0 < NJ; j0 += 2) {
+                    uint32_t x[4];
+                    ldsm_x4(x, sB + (wn * WC + (j0 + (lm >> 1)) * 8 + lr) * S::kBRow + kb * 32 + (lm & 1) * 16);
+                    bf[j0][0] = x[0];
+                    bf[j0][1] = x[1];
+                    bf[j0 + 1][0] = x[2];
+                    bf[j0 + 1][1] = x[3];
                 }
             }
-            // activation scales (rows g, g+8 of each m16) and weight scales (cols 2c, 2c+1 of each n8)
-            float da[MI][2];
-            int sa[MI][2];
-#pragma unroll
-            for (int i = 0; i < MI; ++i)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int r = wm * WR + i * 16 + g + h * 8;
-                    da[i][h] = sAd[r * kKB + kb];
-                    sa[i][h] = Q4 ? sAs[r * kKB + kb] : 0;
-                }
             float dw[NJ][2];
 #pragma unroll
             for (int j = 0; j < NJ; ++j)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) dw[j][h] = scale_to_f32(sBd[(wn * WC + j * 8 + 2 * c + h) * kKB + kb], sbf);
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t wd = (kb < 2) ? dwr[j][h].x : dwr[j][h].y;
+                    dw[j][h] = scale_to_f32((uint16_t)((kb & 1) ? wd >> 16 : wd & 0xffffu), sbf);
+                }
 #pragma unroll
-            for (int i = 0; i < MI; ++i)
+            for (int i = 0; i < MI; ++i) {
+                uint32_t af[4];  // (rows 0-7, bytes 0-15), (8-15, 0-15), (0-7, 16-31), (8-15, 16-31)
+                ldsm_x4(af, sA + (wm * WR + i * 16 + (lm & 1) * 8 + lr) * S::kARow + kb * 32 + (lm >> 1) * 16);
+                const int r = wm * WR + i * 16 + g;
+                const float d0 = sAd[r * kKB + kb], d1 = sAd[(r + 8) * kKB + kb];
+                int cin[4] = {0, 0, 0, 0};
+                if (Q4) {  // nibble bias: -8 * (sum of the token's block), through the MMA's C input
+                    const int s0 = -8 * sAs[r * kKB + kb], s1 = -8 * sAs[(r + 8) * kKB + kb];
+                    cin[0] = s0; cin[1] = s0; cin[2] = s1; cin[3] = s1;
+                }
 #pragma unroll
                 for (int j = 0; j < NJ; ++j) {
                     int d[4];
-                    mma_s8<Q4>(d, af[i], bf[j]);
-                    // d0,d1: row g, cols 2c,2c+1; d2,d3: row g+8
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int h = q >> 1, cl = q & 1;
-                        const int is = d[q] - (Q4 ? 8 * sa[i][h] : 0);
-                        acc[i][j][q] += ((float)is * dw[j][cl]) * da[i][h];
-                    }
+                    mma_a8<Q4>(d, af, bf[j], cin);
+                    // d0,d1: token row g, cols 2c,2c+1; d2,d3: token row g+8
+                    acc[i][j][0] += ((float)d[0] * dw[j][0]) * d0;
+                    acc[i][j][1] += ((float)d[1] * dw[j][1]) * d0;
+                    acc[i][j][2] += ((float)d[2] * dw[j][0]) * d1;
+                    acc[i][j][3] += ((float)d[3] * dw[j][1]) * d1;
                 }
+            }
         }
     }
     cp_async_wait<0>();
@@ -625,44 +665,77 @@ __global__ void __launch_bounds__(kThreads) grouped_gemm_wm_kernel(const GemmPar
         const uint16_t* sWd = reinterpret_cast<const uint16_t*>(base + S::kW + S::kX);
         const float* sXd = reinterpret_cast<const float*>(base + S::kW + S::kX + S::kWd);
         const int32_t* sXs = reinterpret_cast<const int32_t*>(base + S::kW + S::kX + S::kWd + S::kXd);
-#pragma unroll 2
-        for (int kb = 0; kb < kKB; ++kb) {
-            uint32_t af[4];
-            {
-                const uint32_t* w0 = reinterpret_cast<const uint32_t*>(sW + r0 * S::kWRow + kb * (Q4 ? 16 : 32));
-                const uint32_t* w1 = reinterpret_cast<const uint32_t*>(sW + (r0 + 8) * S::kWRow + kb * (Q4 ? 16 : 32));
-                if (Q4) {  // word c: low nibbles -> k 4c.., high nibbles -> k 16+4c..
-                    const uint32_t x0 = w0[c], x1 = w1[c];
-                    af[0] = x0 & 0x0f0f0f0fu;
-                    af[1] = x1 & 0x0f0f0f0fu;
-                    af[2] = (x0 >> 4) & 0x0f0f0f0fu;
-                    af[3] = (x1 >> 4) & 0x0f0f0f0fu;
-                } else {
-                    af[0] = w0[c];
-                    af[1] = w1[c];
-                    af[2] = w0[4 + c];
-                    af[3] = w1[4 + c];
+        // per-stage scales: the weight rows' 4 block scales (8 B each row), the tokens' 4
+        // block scales and sums (16 B each token)
+        float dw0[kKB], dw1[kKB];
+        {
+            const uint2 s0 = *reinterpret_cast<const uint2*>(sWd + r0 * kKB);
+            const uint2 s1 = *reinterpret_cast<const uint2*>(sWd + (r0 + 8) * kKB);
+            const uint16_t h0[4] = {(uint16_t)(s0.x & 0xffff), (uint16_t)(s0.x >> 16), (uint16_t)(s0.y & 0xffff),
+                                    (uint16_t)(s0.y >> 16)};
+            const uint16_t h1[4] = {(uint16_t)(s1.x & 0xffff), (uint16_t)(s1.x >> 16), (uint16_t)(s1.y & 0xffff),
+                                    (uint16_t)(s1.y >> 16)};
+#pragma unroll
+            for (int kb = 0; kb < kKB; ++kb) {
+                dw0[kb] = scale_to_f32(h0[kb], sbf);
+                dw1[kb] = scale_to_f32(h1[kb], sbf);
+            }
+        }
+        float4 da[NJ][2];
+        int4 sb[NJ][2];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int t = j * 8 + 2 * c + h;
+                da[j][h] = *reinterpret_cast<const float4*>(sXd + t * kKB);
+                if (Q4) {
+                    const int4 v = *reinterpret_cast<const int4*>(sXs + t * kKB);
+                    sb[j][h] = make_int4(-8 * v.x, -8 * v.y, -8 * v.z, -8 * v.w);  // nibble bias removal
                 }
             }
-            const float dw0 = scale_to_f32(sWd[r0 * kKB + kb], sbf), dw1 = scale_to_f32(sWd[(r0 + 8) * kKB + kb], sbf);
+        // fragments through ldmatrix: lane l addresses row (l & 7) of matrix (l >> 3)
+        const int lm = lane >> 3, lr = lane & 7;
+#pragma unroll
+        for (int kp = 0; kp < kKB; kp += 2) {
+            uint32_t af[2][4];
+            if (Q4) {  // matrices: rows 0-7 / 8-15 of the warp's m16, blocks kp / kp+1 (16 B each)
+                uint32_t x[4];
+                ldsm_x4(x, sW + (warp * 16 + (lm & 1) * 8 + lr) * S::kWRow + (kp + (lm >> 1)) * 16);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {  // word c: low nibbles -> k 4c.., high nibbles -> k 16+4c..
+                    af[q][0] = x[2 * q] & 0x0f0f0f0fu;
+                    af[q][1] = x[2 * q + 1] & 0x0f0f0f0fu;
+                    af[q][2] = (x[2 * q] >> 4) & 0x0f0f0f0fu;
+                    af[q][3] = (x[2 * q + 1] >> 4) & 0x0f0f0f0fu;
+                }
+            } else {  // one block = rows 0-7 / 8-15 x bytes 0-15 / 16-31
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+                    ldsm_x4(af[q], sW + (warp * 16 + (lm & 1) * 8 + lr) * S::kWRow + (kp + q) * 32 + (lm >> 1) * 16);
+            }
 #pragma unroll
             for (int j = 0; j < NJ; ++j) {
-                const int t0 = j * 8 + 2 * c;  // this thread's tokens t0, t0 + 1
-                const uint32_t* xr = reinterpret_cast<const uint32_t*>(sX + (j * 8 + g) * S::kXRow + kb * 32);
-                const uint32_t bf[2] = {xr[c], xr[4 + c]};
-                const float da0 = sXd[t0 * kKB + kb], da1 = sXd[(t0 + 1) * kKB + kb];
-                int cin[4] = {0, 0, 0, 0};
-                if (Q4) {  // remove the nibble bias: -8 * (sum of the token's block)
-                    const int s0 = -8 * sXs[t0 * kKB + kb], s1 = -8 * sXs[(t0 + 1) * kKB + kb];
-                    cin[0] = s0; cin[1] = s1; cin[2] = s0; cin[3] = s1;
+                uint32_t bx[4];  // tokens j*8.. : (block kp, bytes 0-15), (kp, 16-31), (kp+1, 0-15), (kp+1, 16-31)
+                ldsm_x4(bx, sX + (j * 8 + lr) * S::kXRow + kp * 32 + lm * 16);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int kb = kp + q;
+                    const uint32_t bf[2] = {bx[2 * q], bx[2 * q + 1]};
+                    const float da0 = f4_get(da[j][0], kb), da1 = f4_get(da[j][1], kb);
+                    int cin[4] = {0, 0, 0, 0};
+                    if (Q4) {
+                        const int s0 = i4_get(sb[j][0], kb), s1 = i4_get(sb[j][1], kb);
+                        cin[0] = s0; cin[1] = s1; cin[2] = s0; cin[3] = s1;
+                    }
+                    int d[4];
+                    mma_w<Q4>(d, af[q], bf, cin);
+                    // d0: (row r0, token t0), d1: (r0, t0+1), d2: (r0+8, t0), d3: (r0+8, t0+1)
+                    acc[j][0] += ((float)d[0] * dw0[kb]) * da0;
+                    acc[j][1] += ((float)d[1] * dw0[kb]) * da1;
+                    acc[j][2] += ((float)d[2] * dw1[kb]) * da0;
+                    acc[j][3] += ((float)d[3] * dw1[kb]) * da1;
                 }
-                int d[4];
-                mma_w<Q4>(d, af, bf, cin);
-                // d0: (row r0, token t0), d1: (r0, t0+1), d2: (r0+8, t0), d3: (r0+8, t0+1)
-                acc[j][0] += ((float)d[0] * dw0) * da0;
-                acc[j][1] += ((float)d[1] * dw0) * da1;
-                acc[j][2] += ((float)d[2] * dw1) * da0;
-                acc[j][3] += ((float)d[3] * dw1) * da1;
             }
         }
     }
