@@ -14,7 +14,7 @@
 #include "../../include/moe_b200.h"
 #include "common.cuh"
 #include "moe_decode_sk.cuh"
-#include "moe_gemm.cuh"
+#include "moe_gemm_tc.cuh"
 
 using namespace moe;
 
@@ -76,6 +76,7 @@ struct moe_engine {
     int64_t gemm_min_tokens = 8;  // forwards with more tokens take the grouped-GEMM path
     int32_t decode_flags = kFlagEvictFirst;
     int32_t gemm_bm = 0;  // grouped-GEMM tile kind (gemm_tile_rows codes); 0 = by tokens per expert
+    int64_t tc_min_per_expert = 48;  // tcgen05 bf16 GEMMs from this many expected tokens per expert
     int32_t dist_min_blocks = -1;  // decode: requantise h before the barrier from this many blocks (-1: 2 x SMs)
     // grouped-GEMM path workspace (one allocation, carved per call)
     uint8_t* gws = nullptr;
@@ -640,6 +641,7 @@ struct GemmWs {
     int8_t *xq, *hq;
     float *xd, *hd, *out;
     int32_t *xs, *hs;
+    __nv_bfloat16 *xa, *ha;
 };
 
 int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
@@ -652,6 +654,7 @@ int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
     const size_t o_xq = take(T * H), o_xd = take(T * (H / 32) * 4), o_xs = take(T * (H / 32) * 4);
     const size_t o_hq = take(TK * I), o_hd = take(TK * (I / 32) * 4), o_hs = take(TK * (I / 32) * 4);
     const size_t o_out = take(TK * H * 4);
+    const size_t o_xa = take(T * H * 2), o_ha = take(TK * I * 2);  // bf16 operands of the tcgen05 path
     if (off > eng->gws_bytes) {
         CUDA_TRY(cudaDeviceSynchronize());
         if (eng->gws) CUDA_TRY(cudaFree(eng->gws));
@@ -674,16 +677,71 @@ int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
     w.hd = reinterpret_cast<float*>(b + o_hd);
     w.hs = reinterpret_cast<int32_t*>(b + o_hs);
     w.out = reinterpret_cast<float*>(b + o_out);
+    w.xa = reinterpret_cast<__nv_bfloat16*>(b + o_xa);
+    w.ha = reinterpret_cast<__nv_bfloat16*>(b + o_ha);
     return MOE_OK;
 }
 
 // GEMM tile kind from the expected tokens per active expert (uniform routing): up to 24,
 // the weights-on-M kernel with 8- or 16-token tiles; above, 32- or 64-token M tiles.
-// Codes: -8 / -16 weights-on-M, 16 / 32 / 64 tokens-on-M.
+// Codes: -8 / -16 weights-on-M, 16 / 32 / 64 tokens-on-M, 128 the tcgen05 bf16 kernels.
 int gemm_tile_rows(const moe_engine* eng, int64_t TK) {
     if (eng->gemm_bm) return eng->gemm_bm;
     const int64_t per_expert = TK / std::max<int64_t>(1, std::min<int64_t>(eng->cfg.num_experts, TK));
+    if (per_expert >= eng->tc_min_per_expert) return 128;
     return per_expert <= 6 ? -8 : (per_expert <= 24 ? -16 : (per_expert <= 40 ? 32 : 64));
+}
+
+template <bool Q4>
+int launch_gemms_tc(moe_engine* eng, const GemmWs& w, const void* x, int act_bf16, int64_t T, int64_t K,
+                    cudaStream_t st) {
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    const int64_t TK = T * K;
+    {
+        const int nb = (int)(T * (H / 32));
+        gemm::quant_rows_bf16_kernel<<<std::min((nb + 255) / 256, eng->num_sms * 8), 256, 0, st>>>(
+            static_cast<const uint8_t*>(x), act_bf16, (int)T, H, w.xa);
+        CUDA_TRY(cudaGetLastError());
+    }
+    const int smem = gemm::kStagesTc * gemm::StageTc<Q4>::kBytes + 1024;
+    static thread_local int smem_set[2][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto k1 = gemm::grouped_gemm_tc_kernel<Q4, true>;
+    auto k2 = gemm::grouped_gemm_tc_kernel<Q4, false>;
+    if (dev < 64 && smem_set[1][dev] < smem) {
+        CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        smem_set[1][dev] = smem;
+    }
+    if (dev < 64 && smem_set[0][dev] < smem) {
+        CUDA_TRY(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        smem_set[0][dev] = smem;
+    }
+    const int64_t mt_bound = (TK + gemm::kTcM - 1) / gemm::kTcM + std::min<int64_t>(E, TK);
+    gemm::TcParams tp{};
+    tp.scale_bf16 = eng->scale_bf16;
+    tp.counts = w.counts;
+    tp.starts = w.starts;
+    tp.mtile_start = w.mtile;
+    tp.tokmap = w.tokmap;
+    tp.topk = (int)K;
+    tp.E = E;
+    tp.err = eng->err;
+    gemm::TcParams t1 = tp;  // gate_up: A = token rows, B = unit records (2 rows each)
+    t1.a = w.xa;
+    t1.wbase = eng->gu; t1.rec = eng->unit_bytes(); t1.rows_per_rec = 2; t1.rs = eng->rs1;
+    t1.sc_off = 2 * eng->rs1; t1.ss = eng->ss1; t1.nrec = I; t1.K = H; t1.N = 2 * I;
+    t1.ha = w.ha;
+    k1<<<(unsigned)(mt_bound * (2 * I / gemm::kTcN)), 256, smem, st>>>(t1);
+    CUDA_TRY(cudaGetLastError());
+    gemm::TcParams t2 = tp;  // down: A = bf16 h rows, B = down row records
+    t2.a = w.ha;
+    t2.wbase = eng->dn; t2.rec = eng->row_bytes(); t2.rows_per_rec = 1; t2.rs = eng->rs2;
+    t2.sc_off = eng->rs2; t2.ss = eng->ss2; t2.nrec = H; t2.K = I; t2.N = H;
+    t2.out = w.out;
+    k2<<<(unsigned)(mt_bound * (H / gemm::kTcN)), 256, smem, st>>>(t2);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
 }
 
 template <bool Q4, int BT>
@@ -753,6 +811,10 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
                                                                                   w.mtile, std::abs(gemm_tile_rows(eng, TK)));
     gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk, w.starts, w.smap, w.tokmap);
+    const int bm = gemm_tile_rows(eng, TK);
+    if (bm == 128) {
+        if (int rc = launch_gemms_tc<Q4>(eng, w, x, act_bf16, T, K, st)) return rc;
+    } else {
     {
         const int nb = (int)(T * (H / 32));
         gemm::quant_rows_kernel<Q4><<<std::min((nb + 255) / 256, eng->num_sms * 8), 256, 0, st>>>(
@@ -777,7 +839,6 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     g2.wbase = eng->dn; g2.rec = eng->row_bytes(); g2.rows_per_rec = 1; g2.rs = eng->rs2;
     g2.sc_off = eng->rs2; g2.ss = eng->ss2; g2.nrec = H; g2.K = I; g2.N = H;
     g2.out = w.out;
-    const int bm = gemm_tile_rows(eng, TK);
     int rc;
     switch (bm) {
         case -8: rc = launch_gemms_wm<Q4, 8>(eng, g1, g2, TK, st); break;
@@ -787,6 +848,7 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
         default: rc = launch_gemms<Q4, 64>(eng, g1, g2, TK, st); break;
     }
     if (rc) return rc;
+    }
     {
         const int64_t total = T * (H / 4);
         gemm::combine_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, eng->num_sms * 16), 256, 0, st>>>(
@@ -826,11 +888,12 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (const char* v = std::getenv("MOE_GEMM_MIN_TOKENS")) eng->gemm_min_tokens = std::atoll(v);
     if (const char* v = std::getenv("MOE_DIST_REQUANT_MIN")) eng->dist_min_blocks = std::atoi(v);
     if (const char* v = std::getenv("MOE_DECODE_FLAGS")) eng->decode_flags = std::atoi(v);
+    if (const char* v = std::getenv("MOE_TC_MIN_PER_EXPERT")) eng->tc_min_per_expert = std::atoll(v);
     if (const char* v = std::getenv("MOE_GEMM_BM")) {  // "w8" / "w16" weights-on-M, "16" / "32" / "64"
         const bool wm = v[0] == 'w';
         const int bm = std::atoi(wm ? v + 1 : v);
         if (wm && (bm == 8 || bm == 16)) eng->gemm_bm = -bm;
-        else if (!wm && (bm == 16 || bm == 32 || bm == 64)) eng->gemm_bm = bm;
+        else if (!wm && (bm == 16 || bm == 32 || bm == 64 || bm == 128)) eng->gemm_bm = bm;
     }
     if (const char* v = std::getenv("MOE_DECODE_SK")) eng->use_sk = std::atoi(v) != 0;
     if (const char* v = std::getenv("MOE_SK_COST_A")) eng->sk_cost_a = std::max(0, std::atoi(v));

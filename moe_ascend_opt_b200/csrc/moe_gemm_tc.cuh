@@ -1,0 +1,374 @@
+// Grouped GEMMs of the fused MoE layer on the 5th-generation tensor cores (tcgen05 +
+// TMEM), for many tokens per expert.
+//
+// Arithmetic.  The reference folds every 32-block's integer dot with two fp32 scales
+// (gemm_kernels.cpp:66-186), which keeps the int8 MMA kernels of moe_gemm.cuh busy on the
+// CUDA cores.  Here both operands are dequantised once into bf16 instead:
+//   A  = bf16(q_a * d_a): the token rows after the reference's Q8_0 activation
+//        quantisation (gemm_kernels.cpp:25-58), resp. h after its requantisation
+//        (gemm_kernels.cpp:394-425) -- the reference's quantisation noise is reproduced,
+//        only rounded to bf16;
+//   B  = bf16(q_w * d_w) (Q4_0: (nibble - 8) * d_w), dequantised in shared memory;
+// and the contraction runs in bf16 x bf16 -> fp32 on tcgen05.mma (kind::f16), one
+// accumulator tile of 128 token rows x 128 weight rows in TMEM.  The result equals the
+// reference's to the bf16 rounding of the operands (tolerance parity, not bit-exact).
+//
+// Tile schedule: one CTA per (expert, 128-token tile, 128-weight-row tile), 256 threads.
+// K is streamed in steps of 64 elements (one 128-byte swizzle atom per row):
+//   cp.async  A rows (gathered token rows, bf16) straight into the SWIZZLE_128B K-major
+//             layout, and the raw quantised B rows + their block scales into a staging
+//             buffer, kStagesTc steps ahead;
+//   dequant   every thread expands half a B row (one 32-block) into the bf16 B tile;
+//   mma       one thread issues 4 x tcgen05.mma (K = 16 each) and commits to the
+//             stage's mbarrier, which the refill of that stage waits on (bounded).
+// Epilogue: warps w and w+4 read TMEM lane quarter w%4, columns [64*(w/4), +64):
+//   gate_up  columns interleave (gate, up) per unit, so a thread holds 32 units of its
+//            token: SiLU(gate)*up, the Q8_0 requantisation of that 32-unit block, and
+//            bf16(q_h * d_h) as the down GEMM's A row;
+//   down     fp32 rows of out[pos][n], combined by combine_kernel.
+// No multicast, no cluster, one GPU's memory only.
+#pragma once
+#include "moe_gemm.cuh"
+
+namespace moe {
+namespace gemm {
+
+constexpr int kTcM = 128, kTcN = 128, kTcK = 64;  // tile rows (tokens), cols (weight rows), K step
+constexpr int kStagesTc = 4;
+
+template <bool Q4>
+struct StageTc {
+    static constexpr int kA = kTcM * 128;                // bf16 A tile, 128 B per row (SW128 K-major)
+    static constexpr int kB = kTcN * 128;                // bf16 B tile
+    static constexpr int kRawRow = Q4 ? 32 : 64;         // quantised bytes of one row per step
+    static constexpr int kRaw = kTcN * kRawRow;          // staged raw B rows
+    static constexpr int kSc = kTcN * 4;                 // 2 block scales (fp16/bf16) per row
+    static constexpr int kBytes = (kA + kB + kRaw + kSc + 1023) / 1024 * 1024;  // stages stay 1024-aligned
+};
+
+// ---------------------------------------------------------------- tcgen05 helpers
+// Shared-memory matrix descriptor, SWIZZLE_128B, K-major: start address >> 4 (bits 0-13),
+// leading byte offset (ignored for swizzled K-major, 16 B) >> 4 (bits 16-29), stride byte
+// offset = 1024 B between 8-row groups >> 4 (bits 32-45), descriptor version 1 (bits
+// 46-47), base offset 0, layout type 2 = SWIZZLE_128B (bits 61-63).
+MOE_DEV uint64_t tc_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)(16u >> 4) << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1), B bf16
+// (bits 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+__host__ __device__ constexpr uint32_t tc_idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+MOE_DEV void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
+MOE_DEV void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+MOE_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+MOE_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+MOE_DEV void tc_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+MOE_DEV void cp_async4(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+// Token rows -> bf16(q * d) with the reference's Q8_0 rule (thread per 32-block).
+__global__ void quant_rows_bf16_kernel(const uint8_t* x, int act_bf16, int rows, int cols, __nv_bfloat16* out) {
+    const int nblk = rows * (cols >> 5);
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < nblk; g += gridDim.x * blockDim.x) {
+        const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)g * 64);
+        float v[32];
+        float amax = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 r = __ldg(src + k);
+            const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[8 * k + 2 * i] = scale_to_f32((uint16_t)(w4[i] & 0xffffu), act_bf16);
+                v[8 * k + 2 * i + 1] = scale_to_f32((uint16_t)(w4[i] >> 16), act_bf16);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        const float dd = q8_scale(amax);
+        const float id = q8_inv(dd);
+        uint32_t packed[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+            const __nv_bfloat162 b = __floats2bfloat162_rn((float)q8_quant(v[e], id) * dd, (float)q8_quant(v[e + 1], id) * dd);
+            packed[e / 2] = *reinterpret_cast<const uint32_t*>(&b);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + (size_t)g * 32);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(packed[4 * k], packed[4 * k + 1], packed[4 * k + 2], packed[4 * k + 3]);
+    }
+}
+
+struct TcParams {
+    const __nv_bfloat16* a;  // gate_up: token rows [T][K] (gathered through tokmap/topk); down: position rows [P][K]
+    const uint8_t* wbase;    // weight records, as GemmParams
+    int64_t rec;
+    int rows_per_rec, rs, sc_off, ss, nrec, K, N, scale_bf16;
+    const int32_t* counts;
+    const int32_t* starts;
+    const int32_t* mtile_start;  // tiles of kTcM rows per expert
+    const int32_t* tokmap;
+    int topk, E;
+    __nv_bfloat16* ha;  // gate_up output: bf16(q_h * d_h) [P][I]
+    float* out;         // down output: [P][H]
+    int32_t* err;
+};
+
+template <bool Q4, bool GATE_UP>
+__global__ void __launch_bounds__(256, 1) grouped_gemm_tc_kernel(const TcParams p) {
+    using S = StageTc<Q4>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the swizzled tiles need 1024-byte alignment
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t s_bar[kStagesTc];
+    __shared__ uint32_t s_tmem;
+    __shared__ int64_t s_arow[kTcM];
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const int ntiles_n = p.N / kTcN;
+    const int mt_total = p.mtile_start[p.E];
+    const int tile = blockIdx.x;
+    if (tile >= mt_total * ntiles_n) return;
+    const int mt_glob = tile / ntiles_n, nt = tile % ntiles_n;
+    int lo = 0, hi = p.E;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (p.mtile_start[mid] <= mt_glob) lo = mid;
+        else hi = mid;
+    }
+    const int e = lo;
+    const int m0 = (mt_glob - p.mtile_start[e]) * kTcM;
+    const int cnt = p.counts[e];
+    const int pos0 = p.starts[e] + m0;
+    const int mrows = min(kTcM, cnt - m0);
+    const int nsteps = p.K / kTcK;
+    const uint8_t* wexp = p.wbase + (int64_t)e * p.nrec * p.rec;
+
+    for (int r = tid; r < kTcM; r += 256) {
+        const int pos = pos0 + min(r, max(mrows, 1) - 1);
+        s_arow[r] = GATE_UP ? (int64_t)(p.tokmap[pos] / p.topk) : (int64_t)pos;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < kStagesTc; ++s) mbar_init(&s_bar[s], 1);
+        s_ok = 1;
+    }
+    if (warp == 0) {  // TMEM: 128 fp32 columns x 128 lanes for the accumulator tile
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(smem_u32(&s_tmem))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_barrier_init();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    // weight row n (0..127) of this tile -> offsets of its quants and its scale field
+    auto w_row = [&](int n, int64_t& qoff, int64_t& soff) {
+        const int64_t gn = (int64_t)nt * kTcN + n;
+        const int64_t rec = gn / p.rows_per_rec, sub = gn - rec * p.rows_per_rec;
+        qoff = rec * p.rec + sub * p.rs;
+        soff = rec * p.rec + p.sc_off + sub * p.ss;
+    };
+    auto load_stage = [&](int st, int ks) {
+        uint8_t* base = smem + (size_t)st * S::kBytes;
+        uint8_t* sA = base;
+        uint8_t* sRaw = base + S::kA + S::kB;
+        uint8_t* sSc = sRaw + S::kRaw;
+        // A: 128 rows x 8 chunks of 16 B, chunk c of row r at position c ^ (r & 7)
+        for (int ch = tid; ch < kTcM * 8; ch += 256) {
+            const int r = ch >> 3, c = ch & 7;
+            const __nv_bfloat16* src = p.a + s_arow[r] * p.K + (int64_t)ks * kTcK + c * 8;
+            cp_async16(sA + r * 128 + ((c ^ (r & 7)) << 4), src, r < mrows);
+        }
+        // raw B rows (Q4: 2 x 16 B, Q8: 4 x 16 B) and 2 block scales (4 B)
+        constexpr int kChunks = S::kRawRow / 16;
+        for (int ch = tid; ch < kTcN * kChunks; ch += 256) {
+            const int n = ch / kChunks, c = ch % kChunks;
+            int64_t qo, so;
+            w_row(n, qo, so);
+            cp_async16(sRaw + n * S::kRawRow + c * 16, wexp + qo + (int64_t)ks * S::kRawRow + c * 16, true);
+        }
+        for (int n = tid; n < kTcN; n += 256) {
+            int64_t qo, so;
+            w_row(n, qo, so);
+            cp_async4(sSc + n * 4, wexp + so + (int64_t)ks * 4);
+        }
+    };
+
+    const uint32_t idesc = tc_idesc_bf16(kTcM, kTcN);
+    const bool sbf = p.scale_bf16 != 0;
+    for (int s = 0; s < kStagesTc - 1; ++s) {
+        if (s < nsteps) load_stage(s, s);
+        cp_async_commit();
+    }
+    bool ok = true;
+    for (int s = 0; s < nsteps; ++s) {
+        const int st = s % kStagesTc;
+        uint8_t* base = smem + (size_t)st * S::kBytes;
+        cp_async_wait<kStagesTc - 2>();
+        __syncthreads();
+        {   // dequantise B: thread -> (row tid/2, 32-block tid%2) -> 16 bf16 pairs = 4 chunks
+            const int n = tid >> 1, h = tid & 1;
+            const uint8_t* raw = base + S::kA + S::kB + n * S::kRawRow + h * (Q4 ? 16 : 32);
+            const uint16_t scb = reinterpret_cast<const uint16_t*>(base + S::kA + S::kB + S::kRaw + n * 4)[h];
+            const float dw = scale_to_f32(scb, sbf);
+            uint32_t pk[16];
+            if (Q4) {  // word i = elements 8i..8i+7, nibble j = element 8i+j, value nibble - 8
+                const uint4 q = *reinterpret_cast<const uint4*>(raw);
+                const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; j += 2) {
+                        const float v0 = (float)((int)((qq[i] >> (4 * j)) & 15u) - 8) * dw;
+                        const float v1 = (float)((int)((qq[i] >> (4 * j + 4)) & 15u) - 8) * dw;
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(v0, v1);
+                        pk[4 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
+                    }
+            } else {  // word i = elements 4i..4i+3 (int8)
+                const uint4 q0 = reinterpret_cast<const uint4*>(raw)[0], q1 = reinterpret_cast<const uint4*>(raw)[1];
+                const uint32_t qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; j += 2) {
+                        const float v0 = (float)(int8_t)((qq[i] >> (8 * j)) & 0xffu) * dw;
+                        const float v1 = (float)(int8_t)((qq[i] >> (8 * j + 8)) & 0xffu) * dw;
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(v0, v1);
+                        pk[2 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
+                    }
+            }
+            uint8_t* rowp = base + S::kA + n * 128;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                *reinterpret_cast<uint4*>(rowp + (((4 * h + i) ^ (n & 7)) << 4)) =
+                    make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+        // generic-proxy writes (cp.async A, the dequantised B) -> visible to the tensor core
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t sa = smem_u32(base), sb = smem_u32(base + S::kA);
+#pragma unroll
+            for (int k = 0; k < kTcK / 16; ++k)  // K = 16 per MMA: advance 32 B inside the swizzle atom
+                tc_mma(tmem, tc_desc_sw128(sa + 32 * k), tc_desc_sw128(sb + 32 * k), idesc, s > 0 || k > 0);
+            tc_commit(&s_bar[st]);
+        }
+        // refill: step s + kStagesTc - 1 goes to the stage last read by the MMAs of step s - 1
+        if (s >= 1) {
+            const int ps = s - 1;
+            if (!mbar_wait(&s_bar[ps % kStagesTc], (uint32_t)(ps / kStagesTc) & 1u)) ok = false;
+        }
+        if (s + kStagesTc - 1 < nsteps) load_stage((s + kStagesTc - 1) % kStagesTc, s + kStagesTc - 1);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    {   // every MMA of the tile has completed once the last step's commit has arrived
+        const int ls = nsteps - 1;
+        if (!mbar_wait(&s_bar[ls % kStagesTc], (uint32_t)(ls / kStagesTc) & 1u)) ok = false;
+    }
+    if (!ok) {  // a commit did not arrive in time: flag it, give the MMAs one more bounded wait
+        atomicExch(p.err, kErrFullWait);
+        s_ok = 0;
+        const int ls = nsteps - 1;
+        mbar_wait(&s_bar[ls % kStagesTc], (uint32_t)(ls / kStagesTc) & 1u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // ---------------- epilogue: lane quarter warp%4, columns [64*(warp/4), +64) ----------------
+    if (s_ok) {
+        const int r = (warp & 3) * 32 + lane;  // token row of the tile (TMEM lane)
+        const int c0 = (warp >> 2) * 64;
+        const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0;
+        float v[64];
+        {
+            float t0[32], t1[32];
+            tc_ld32(taddr, t0);
+            tc_ld32(taddr + 32, t1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) { v[i] = t0[i]; v[32 + i] = t1[i]; }
+        }
+        if (r < mrows) {
+            const int pos = pos0 + r;
+            if (GATE_UP) {  // columns (2u, 2u+1) = (gate, up) of unit u0 + u
+                const int I = p.N / 2;
+                const int u0 = nt * (kTcN / 2) + c0 / 2;  // a 32-unit block
+                float hv[32];
+                float amax = 0.f;
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    hv[u] = silu_mul(v[2 * u], v[2 * u + 1]);
+                    amax = fmaxf(amax, fabsf(hv[u]));
+                }
+                const float dd = q8_scale(amax);
+                const float id = q8_inv(dd);
+                uint32_t pk[16];
+#pragma unroll
+                for (int u = 0; u < 32; u += 2) {
+                    const __nv_bfloat162 b2 =
+                        __floats2bfloat162_rn((float)q8_quant(hv[u], id) * dd, (float)q8_quant(hv[u + 1], id) * dd);
+                    pk[u / 2] = *reinterpret_cast<const uint32_t*>(&b2);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(p.ha + (int64_t)pos * I + u0);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) dst[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+            } else {
+                float4* dst = reinterpret_cast<float4*>(p.out + (int64_t)pos * p.N + nt * kTcN + c0);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) dst[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem) : "memory");
+    }
+}
+
+}  // namespace gemm
+}  // namespace moe

@@ -261,7 +261,7 @@ def test_split_k_kernel_matches_barrier_kernel(qt, E, H, I, T, K, monkeypatch):
     assert rel <= 2e-3 and cos >= MIN_COS, (rel, cos)
 
 
-@pytest.mark.parametrize("bm", ["w8", "w16", "16", "32", "64"])
+@pytest.mark.parametrize("bm", ["w8", "w16", "16", "32", "64", "128"])
 @pytest.mark.parametrize("qt", [0, 1])
 def test_gemm_tile_rows_variants(qt, bm, monkeypatch):
     # every token-tile height of the grouped GEMM, on ragged per-expert counts
