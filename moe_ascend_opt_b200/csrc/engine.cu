@@ -732,14 +732,14 @@ int launch_gemms_tc(moe_engine* eng, const GemmWs& w, const void* x, int act_bf1
     t1.wbase = eng->gu; t1.rec = eng->unit_bytes(); t1.rows_per_rec = 2; t1.rs = eng->rs1;
     t1.sc_off = 2 * eng->rs1; t1.ss = eng->ss1; t1.nrec = I; t1.K = H; t1.N = 2 * I;
     t1.ha = w.ha;
-    k1<<<(unsigned)(mt_bound * (2 * I / gemm::kTcN)), 256, smem, st>>>(t1);
+    k1<<<(unsigned)(mt_bound * (2 * I / gemm::kTcN)), gemm::kTcThreads, smem, st>>>(t1);
     CUDA_TRY(cudaGetLastError());
     gemm::TcParams t2 = tp;  // down: A = bf16 h rows, B = down row records
     t2.a = w.ha;
     t2.wbase = eng->dn; t2.rec = eng->row_bytes(); t2.rows_per_rec = 1; t2.rs = eng->rs2;
     t2.sc_off = eng->rs2; t2.ss = eng->ss2; t2.nrec = H; t2.K = I; t2.N = H;
     t2.out = w.out;
-    k2<<<(unsigned)(mt_bound * (H / gemm::kTcN)), 256, smem, st>>>(t2);
+    k2<<<(unsigned)(mt_bound * (H / gemm::kTcN)), gemm::kTcThreads, smem, st>>>(t2);
     CUDA_TRY(cudaGetLastError());
     return MOE_OK;
 }

@@ -13,14 +13,17 @@
 // accumulator tile of 128 token rows x 128 weight rows in TMEM.  The result equals the
 // reference's to the bf16 rounding of the operands (tolerance parity, not bit-exact).
 //
-// Tile schedule: one CTA per (expert, 128-token tile, 128-weight-row tile), 256 threads.
-// K is streamed in steps of 64 elements (one 128-byte swizzle atom per row):
+// Tile schedule: one CTA per (expert, 128-token tile, 128-weight-row tile), 256 threads,
+// 3 CTAs per SM; K is streamed in steps of 64 elements (one 128-byte swizzle atom per row)
+// through kStagesTc stages:
 //   cp.async  A rows (gathered token rows, bf16) straight into the SWIZZLE_128B K-major
-//             layout, and the raw quantised B rows + their block scales into a staging
-//             buffer, kStagesTc steps ahead;
-//   dequant   every thread expands half a B row (one 32-block) into the bf16 B tile;
-//   mma       one thread issues 4 x tcgen05.mma (K = 16 each) and commits to the
-//             stage's mbarrier, which the refill of that stage waits on (bounded).
+//             layout, one step ahead;
+//   dequant   every thread expands half a B row (one 32-block, loaded into registers two
+//             steps ahead) into the bf16 B tile;
+//   mma       one thread issues 4 x tcgen05.mma (K = 16 each) and commits them to the
+//             stage's mbarrier, which the refill of that stage waits on.
+// (A warp-specialised variant with 3 stages and 2 CTAs per SM measured slower.)
+// All waits are bounded; a wait that runs out sets the error word and the tile is dropped.
 // Epilogue: warps w and w+4 read TMEM lane quarter w%4, columns [64*(w/4), +64):
 //   gate_up  columns interleave (gate, up) per unit, so a thread holds 32 units of its
 //            token: SiLU(gate)*up, the Q8_0 requantisation of that 32-unit block, and
@@ -34,16 +37,14 @@ namespace moe {
 namespace gemm {
 
 constexpr int kTcM = 128, kTcN = 128, kTcK = 64;  // tile rows (tokens), cols (weight rows), K step
-constexpr int kStagesTc = 4;
+constexpr int kStagesTc = 2;  // x 32 KB: with 1 KB alignment slack and 80 registers, 3 CTAs per SM
 
 template <bool Q4>
 struct StageTc {
     static constexpr int kA = kTcM * 128;                // bf16 A tile, 128 B per row (SW128 K-major)
     static constexpr int kB = kTcN * 128;                // bf16 B tile
     static constexpr int kRawRow = Q4 ? 32 : 64;         // quantised bytes of one row per step
-    static constexpr int kRaw = kTcN * kRawRow;          // staged raw B rows
-    static constexpr int kSc = kTcN * 4;                 // 2 block scales (fp16/bf16) per row
-    static constexpr int kBytes = (kA + kB + kRaw + kSc + 1023) / 1024 * 1024;  // stages stay 1024-aligned
+    static constexpr int kBytes = kA + kB;                // 32 KB: stages stay 1024-aligned
 };
 
 // ---------------------------------------------------------------- tcgen05 helpers
@@ -152,13 +153,16 @@ struct TcParams {
     int32_t* err;
 };
 
+constexpr int kTcProducers = 256;  // all threads copy A, dequantise B and run the epilogue
+constexpr int kTcThreads = kTcProducers;
+
 template <bool Q4, bool GATE_UP>
-__global__ void __launch_bounds__(256, 1) grouped_gemm_tc_kernel(const TcParams p) {
+__global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const TcParams p) {
     using S = StageTc<Q4>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzled tiles need 1024-byte alignment
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t s_bar[kStagesTc];
+    __shared__ __align__(8) uint64_t s_empty[kStagesTc], s_done;
     __shared__ uint32_t s_tmem;
     __shared__ int64_t s_arow[kTcM];
     __shared__ int s_ok;
@@ -183,12 +187,13 @@ __global__ void __launch_bounds__(256, 1) grouped_gemm_tc_kernel(const TcParams 
     const int nsteps = p.K / kTcK;
     const uint8_t* wexp = p.wbase + (int64_t)e * p.nrec * p.rec;
 
-    for (int r = tid; r < kTcM; r += 256) {
+    for (int r = tid; r < kTcM; r += kTcThreads) {
         const int pos = pos0 + min(r, max(mrows, 1) - 1);
         s_arow[r] = GATE_UP ? (int64_t)(p.tokmap[pos] / p.topk) : (int64_t)pos;
     }
     if (tid == 0) {
-        for (int s = 0; s < kStagesTc; ++s) mbar_init(&s_bar[s], 1);
+        for (int s = 0; s < kStagesTc; ++s) mbar_init(&s_empty[s], 1);  // tcgen05.commit of the step's MMAs
+        mbar_init(&s_done, 1);
         s_ok = 1;
     }
     if (warp == 0) {  // TMEM: 128 fp32 columns x 128 lanes for the accumulator tile
@@ -212,36 +217,41 @@ __global__ void __launch_bounds__(256, 1) grouped_gemm_tc_kernel(const TcParams 
     auto load_stage = [&](int st, int ks) {
         uint8_t* base = smem + (size_t)st * S::kBytes;
         uint8_t* sA = base;
-        uint8_t* sRaw = base + S::kA + S::kB;
-        uint8_t* sSc = sRaw + S::kRaw;
         // A: 128 rows x 8 chunks of 16 B, chunk c of row r at position c ^ (r & 7)
-        for (int ch = tid; ch < kTcM * 8; ch += 256) {
+        for (int ch = tid; ch < kTcM * 8; ch += kTcProducers) {
             const int r = ch >> 3, c = ch & 7;
             const __nv_bfloat16* src = p.a + s_arow[r] * p.K + (int64_t)ks * kTcK + c * 8;
             cp_async16(sA + r * 128 + ((c ^ (r & 7)) << 4), src, r < mrows);
         }
-        // raw B rows (Q4: 2 x 16 B, Q8: 4 x 16 B) and 2 block scales (4 B)
-        constexpr int kChunks = S::kRawRow / 16;
-        for (int ch = tid; ch < kTcN * kChunks; ch += 256) {
-            const int n = ch / kChunks, c = ch % kChunks;
-            int64_t qo, so;
-            w_row(n, qo, so);
-            cp_async16(sRaw + n * S::kRawRow + c * 16, wexp + qo + (int64_t)ks * S::kRawRow + c * 16, true);
-        }
-        for (int n = tid; n < kTcN; n += 256) {
-            int64_t qo, so;
-            w_row(n, qo, so);
-            cp_async4(sSc + n * 4, wexp + so + (int64_t)ks * 4);
-        }
     };
 
+    // raw B of this thread's (row tid/2, 32-block tid%2) per step, loaded into registers two
+    // steps ahead of its dequantisation (no shared staging: 3 CTAs fit on an SM)
+    struct RawB {
+        uint4 q0, q1;  // Q4: q0 only
+        uint16_t sc;
+    };
+    auto load_raw = [&](int ks, RawB& rb) {
+        const int n = tid >> 1, h = tid & 1;
+        int64_t qo, so;
+        w_row(n, qo, so);
+        const uint4* src = reinterpret_cast<const uint4*>(wexp + qo + (int64_t)ks * S::kRawRow + h * (Q4 ? 16 : 32));
+        rb.q0 = __ldg(src);
+        if (!Q4) rb.q1 = __ldg(src + 1);
+        rb.sc = __ldg(reinterpret_cast<const unsigned short*>(wexp + so) + 2 * ks + h);
+    };
+    RawB rb0{}, rb1{};
+    if (tid < kTcProducers) {
+        if (0 < nsteps) load_raw(0, rb0);
+        if (1 < nsteps) load_raw(1, rb1);
+    }
     const uint32_t idesc = tc_idesc_bf16(kTcM, kTcN);
     const bool sbf = p.scale_bf16 != 0;
+    bool ok = true;
     for (int s = 0; s < kStagesTc - 1; ++s) {
         if (s < nsteps) load_stage(s, s);
         cp_async_commit();
     }
-    bool ok = true;
     for (int s = 0; s < nsteps; ++s) {
         const int st = s % kStagesTc;
         uint8_t* base = smem + (size_t)st * S::kBytes;
@@ -249,31 +259,31 @@ __global__ void __launch_bounds__(256, 1) grouped_gemm_tc_kernel(const TcParams 
         __syncthreads();
         {   // dequantise B: thread -> (row tid/2, 32-block tid%2) -> 16 bf16 pairs = 4 chunks
             const int n = tid >> 1, h = tid & 1;
-            const uint8_t* raw = base + S::kA + S::kB + n * S::kRawRow + h * (Q4 ? 16 : 32);
-            const uint16_t scb = reinterpret_cast<const uint16_t*>(base + S::kA + S::kB + S::kRaw + n * 4)[h];
-            const float dw = scale_to_f32(scb, sbf);
+            const RawB cur = rb0;
+            rb0 = rb1;
+            if (s + 2 < nsteps) load_raw(s + 2, rb1);
+            const float dw = scale_to_f32(cur.sc, sbf);
             uint32_t pk[16];
             if (Q4) {  // word i = elements 8i..8i+7, nibble j = element 8i+j, value nibble - 8
-                const uint4 q = *reinterpret_cast<const uint4*>(raw);
-                const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+                const uint32_t qq[4] = {cur.q0.x, cur.q0.y, cur.q0.z, cur.q0.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
-                    for (int j = 0; j < 8; j += 2) {
-                        const float v0 = (float)((int)((qq[i] >> (4 * j)) & 15u) - 8) * dw;
-                        const float v1 = (float)((int)((qq[i] >> (4 * j + 4)) & 15u) - 8) * dw;
+                    for (int j = 0; j < 8; j += 2) {  // 2^23 + n as float bits, minus 2^23 + 8: exact n - 8
+                        const float v0 = (__uint_as_float(((qq[i] >> (4 * j)) & 15u) | 0x4B000000u) - 8388616.0f) * dw;
+                        const float v1 = (__uint_as_float(((qq[i] >> (4 * j + 4)) & 15u) | 0x4B000000u) - 8388616.0f) * dw;
                         const __nv_bfloat162 b2 = __floats2bfloat162_rn(v0, v1);
                         pk[4 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
                     }
             } else {  // word i = elements 4i..4i+3 (int8)
-                const uint4 q0 = reinterpret_cast<const uint4*>(raw)[0], q1 = reinterpret_cast<const uint4*>(raw)[1];
-                const uint32_t qq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                const uint32_t qq[8] = {cur.q0.x, cur.q0.y, cur.q0.z, cur.q0.w, cur.q1.x, cur.q1.y, cur.q1.z, cur.q1.w};
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
 #pragma unroll
                     for (int j = 0; j < 4; j += 2) {
-                        const float v0 = (float)(int8_t)((qq[i] >> (8 * j)) & 0xffu) * dw;
-                        const float v1 = (float)(int8_t)((qq[i] >> (8 * j + 8)) & 0xffu) * dw;
+                        // byte b ^ 0x80 = q + 128: 2^23 + q + 128 as float bits, minus 2^23 + 128
+                        const float v0 = (__uint_as_float((((qq[i] >> (8 * j)) & 0xffu) ^ 0x80u) | 0x4B000000u) - 8388736.0f) * dw;
+                        const float v1 = (__uint_as_float((((qq[i] >> (8 * j + 8)) & 0xffu) ^ 0x80u) | 0x4B000000u) - 8388736.0f) * dw;
                         const __nv_bfloat162 b2 = __floats2bfloat162_rn(v0, v1);
                         pk[2 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
                     }
@@ -293,33 +303,31 @@ __global__ void __launch_bounds__(256, 1) grouped_gemm_tc_kernel(const TcParams 
 #pragma unroll
             for (int k = 0; k < kTcK / 16; ++k)  // K = 16 per MMA: advance 32 B inside the swizzle atom
                 tc_mma(tmem, tc_desc_sw128(sa + 32 * k), tc_desc_sw128(sb + 32 * k), idesc, s > 0 || k > 0);
-            tc_commit(&s_bar[st]);
+            tc_commit(&s_empty[st]);
         }
         // refill: step s + kStagesTc - 1 goes to the stage last read by the MMAs of step s - 1
         if (s >= 1) {
             const int ps = s - 1;
-            if (!mbar_wait(&s_bar[ps % kStagesTc], (uint32_t)(ps / kStagesTc) & 1u)) ok = false;
+            if (!mbar_wait(&s_empty[ps % kStagesTc], (uint32_t)(ps / kStagesTc) & 1u)) ok = false;
         }
         if (s + kStagesTc - 1 < nsteps) load_stage((s + kStagesTc - 1) % kStagesTc, s + kStagesTc - 1);
         cp_async_commit();
     }
     cp_async_wait<0>();
-    {   // every MMA of the tile has completed once the last step's commit has arrived
-        const int ls = nsteps - 1;
-        if (!mbar_wait(&s_bar[ls % kStagesTc], (uint32_t)(ls / kStagesTc) & 1u)) ok = false;
-    }
-    if (!ok) {  // a commit did not arrive in time: flag it, give the MMAs one more bounded wait
+    if (tid == 0) tc_commit(&s_done);  // arrives once every MMA issued above has completed
+    if (!ok) atomicExch(p.err, kErrFullWait);
+    // bounded wait for the accumulator (on a failure path as well, before TMEM is released)
+    if (!mbar_wait(&s_done, 0u)) {
         atomicExch(p.err, kErrFullWait);
-        s_ok = 0;
-        const int ls = nsteps - 1;
-        mbar_wait(&s_bar[ls % kStagesTc], (uint32_t)(ls / kStagesTc) & 1u);
+        ok = false;
     }
+    if (!ok) s_ok = 0;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
 
     // ---------------- epilogue: lane quarter warp%4, columns [64*(warp/4), +64) ----------------
-    if (s_ok) {
+    if (s_ok && tid < kTcProducers) {
         const int r = (warp & 3) * 32 + lane;  // token row of the tile (TMEM lane)
         const int c0 = (warp >> 2) * 64;
         const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0;
