@@ -40,7 +40,7 @@ METRIC = "fused MoE layer µs & effective weight GB/s vs HBM peak, tokens 1–40
 HBM_FALLBACK = 6650.0
 # DRAM bytes (read + write) per launch of moe_decode_kernel<Q4> at this workload, from the
 # ncu capture summarised in profiles/moe_decode_q4_T1.md.
-NCU_TRAFFIC_BYTES = 21320960
+NCU_TRAFFIC_BYTES = 21330688
 
 
 def peaks():
