@@ -15,7 +15,8 @@ namespace moe {
 // the workspace error word and the kernel leaves without hanging the GPU.
 constexpr uint32_t kSpinLimit = 1u << 22;
 
-enum ErrCode : int32_t { kErrNone = 0, kErrGridBarrier = 1, kErrFullWait = 2, kErrEmptyWait = 3, kErrPeerWait = 4 };
+enum ErrCode : int32_t { kErrNone = 0, kErrGridBarrier = 1, kErrFullWait = 2, kErrEmptyWait = 3, kErrPeerWait = 4,
+                         kErrRange = 5 };
 
 MOE_DEV float act_to_f32(const void* p, int64_t i, int is_bf16) {
     if (is_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);

@@ -641,7 +641,7 @@ struct GemmWs {
     int8_t *xq, *hq;
     float *xd, *hd, *out;
     int32_t *xs, *hs;
-    __nv_bfloat16 *xa, *ha;
+    __half *xa, *ha;
 };
 
 int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
@@ -654,7 +654,7 @@ int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
     const size_t o_xq = take(T * H), o_xd = take(T * (H / 32) * 4), o_xs = take(T * (H / 32) * 4);
     const size_t o_hq = take(TK * I), o_hd = take(TK * (I / 32) * 4), o_hs = take(TK * (I / 32) * 4);
     const size_t o_out = take(TK * H * 4);
-    const size_t o_xa = take(T * H * 2), o_ha = take(TK * I * 2);  // bf16 operands of the tcgen05 path
+    const size_t o_xa = take(T * H * 2), o_ha = take(TK * I * 2);  // fp16 operands of the tcgen05 path
     if (off > eng->gws_bytes) {
         CUDA_TRY(cudaDeviceSynchronize());
         if (eng->gws) CUDA_TRY(cudaFree(eng->gws));
@@ -677,8 +677,8 @@ int gemm_workspace(moe_engine* eng, int64_t T, int64_t K, GemmWs& w) {
     w.hd = reinterpret_cast<float*>(b + o_hd);
     w.hs = reinterpret_cast<int32_t*>(b + o_hs);
     w.out = reinterpret_cast<float*>(b + o_out);
-    w.xa = reinterpret_cast<__nv_bfloat16*>(b + o_xa);
-    w.ha = reinterpret_cast<__nv_bfloat16*>(b + o_ha);
+    w.xa = reinterpret_cast<__half*>(b + o_xa);
+    w.ha = reinterpret_cast<__half*>(b + o_ha);
     return MOE_OK;
 }
 
@@ -699,8 +699,8 @@ int launch_gemms_tc(moe_engine* eng, const GemmWs& w, const void* x, int act_bf1
     const int64_t TK = T * K;
     {
         const int nb = (int)(T * (H / 32));
-        gemm::quant_rows_bf16_kernel<<<std::min((nb + 255) / 256, eng->num_sms * 8), 256, 0, st>>>(
-            static_cast<const uint8_t*>(x), act_bf16, (int)T, H, w.xa);
+        gemm::quant_rows_f16_kernel<<<std::min((nb + 255) / 256, eng->num_sms * 8), 256, 0, st>>>(
+            static_cast<const uint8_t*>(x), act_bf16, (int)T, H, w.xa, eng->err);
         CUDA_TRY(cudaGetLastError());
     }
     const int smem = gemm::kStagesTc * gemm::StageTc<Q4>::kBytes + 1024;

@@ -3,23 +3,26 @@
 //
 // Arithmetic.  The reference folds every 32-block's integer dot with two fp32 scales
 // (gemm_kernels.cpp:66-186), which keeps the int8 MMA kernels of moe_gemm.cuh busy on the
-// CUDA cores.  Here both operands are dequantised once into bf16 instead:
-//   A  = bf16(q_a * d_a): the token rows after the reference's Q8_0 activation
+// CUDA cores.  Here both operands are dequantised once into fp16 instead:
+//   A  = fp16(q_a * d_a): the token rows after the reference's Q8_0 activation
 //        quantisation (gemm_kernels.cpp:25-58), resp. h after its requantisation
 //        (gemm_kernels.cpp:394-425) -- the reference's quantisation noise is reproduced,
-//        only rounded to bf16;
-//   B  = bf16(q_w * d_w) (Q4_0: (nibble - 8) * d_w), dequantised in shared memory;
-// and the contraction runs in bf16 x bf16 -> fp32 on tcgen05.mma (kind::f16), one
+//        only rounded to fp16 (2^-11 relative);
+//   B  = fp16(q_w * d_w) (Q4_0: (nibble - 8) * d_w), dequantised in shared memory;
+// and the contraction runs in fp16 x fp16 -> fp32 on tcgen05.mma (kind::f16), one
 // accumulator tile of 128 token rows x 128 weight rows in TMEM.  The result equals the
-// reference's to the bf16 rounding of the operands (tolerance parity, not bit-exact).
+// reference's to the fp16 rounding of the operands (tolerance parity, not bit-exact).
+// fp16 rather than bf16: bf16's 2^-9 rounding left the FFN output at the edge of the
+// 1e-2 tolerance.  A 32-block whose magnitude exceeds the fp16 range (|x| > 65504) sets
+// device error kErrRange; such activations need the int8 path (MOE_TC_MIN_PER_EXPERT).
 //
 // Tile schedule: one CTA per (expert, 128-token tile, 128-weight-row tile), 256 threads,
 // 3 CTAs per SM; K is streamed in steps of 64 elements (one 128-byte swizzle atom per row)
 // through kStagesTc stages:
-//   cp.async  A rows (gathered token rows, bf16) straight into the SWIZZLE_128B K-major
+//   cp.async  A rows (gathered token rows, fp16) straight into the SWIZZLE_128B K-major
 //             layout, one step ahead;
 //   dequant   every thread expands half a B row (one 32-block, loaded into registers two
-//             steps ahead) into the bf16 B tile;
+//             steps ahead) into the fp16 B tile;
 //   mma       one thread issues 4 x tcgen05.mma (K = 16 each) and commits them to the
 //             stage's mbarrier, which the refill of that stage waits on.
 // (A warp-specialised variant with 3 stages and 2 CTAs per SM measured slower.)
@@ -27,7 +30,7 @@
 // Epilogue: warps w and w+4 read TMEM lane quarter w%4, columns [64*(w/4), +64):
 //   gate_up  columns interleave (gate, up) per unit, so a thread holds 32 units of its
 //            token: SiLU(gate)*up, the Q8_0 requantisation of that 32-unit block, and
-//            bf16(q_h * d_h) as the down GEMM's A row;
+//            fp16(q_h * d_h) as the down GEMM's A row;
 //   down     fp32 rows of out[pos][n], combined by combine_kernel.
 // No multicast, no cluster, one GPU's memory only.
 #pragma once
@@ -41,8 +44,8 @@ constexpr int kStagesTc = 2;  // x 32 KB: with 1 KB alignment slack and 80 regis
 
 template <bool Q4>
 struct StageTc {
-    static constexpr int kA = kTcM * 128;                // bf16 A tile, 128 B per row (SW128 K-major)
-    static constexpr int kB = kTcN * 128;                // bf16 B tile
+    static constexpr int kA = kTcM * 128;                // fp16 A tile, 128 B per row (SW128 K-major)
+    static constexpr int kB = kTcN * 128;                // fp16 B tile
     static constexpr int kRawRow = Q4 ? 32 : 64;         // quantised bytes of one row per step
     static constexpr int kBytes = kA + kB;                // 32 KB: stages stay 1024-aligned
 };
@@ -62,10 +65,10 @@ MOE_DEV uint64_t tc_desc_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1), B bf16
-// (bits 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
-__host__ __device__ constexpr uint32_t tc_idesc_bf16(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor, kind::f16: D fp32 (bits 4-5 = 1), A and B fp16 (bits 7-9 and
+// 10-12 = 0), both K-major (bits 15, 16 = 0), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+__host__ __device__ constexpr uint32_t tc_idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 MOE_DEV void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool accumulate) {
@@ -105,8 +108,8 @@ MOE_DEV void cp_async4(void* smem_dst, const void* gsrc) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
 }
 
-// Token rows -> bf16(q * d) with the reference's Q8_0 rule (thread per 32-block).
-__global__ void quant_rows_bf16_kernel(const uint8_t* x, int act_bf16, int rows, int cols, __nv_bfloat16* out) {
+// Token rows -> fp16(q * d) with the reference's Q8_0 rule (thread per 32-block).
+__global__ void quant_rows_f16_kernel(const uint8_t* x, int act_bf16, int rows, int cols, __half* out, int32_t* err) {
     const int nblk = rows * (cols >> 5);
     for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < nblk; g += gridDim.x * blockDim.x) {
         const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)g * 64);
@@ -124,12 +127,13 @@ __global__ void quant_rows_bf16_kernel(const uint8_t* x, int act_bf16, int rows,
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        if (amax > 65504.f) atomicExch(err, kErrRange);
         const float dd = q8_scale(amax);
         const float id = q8_inv(dd);
         uint32_t packed[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-            const __nv_bfloat162 b = __floats2bfloat162_rn((float)q8_quant(v[e], id) * dd, (float)q8_quant(v[e + 1], id) * dd);
+            const __half2 b = __floats2half2_rn((float)q8_quant(v[e], id) * dd, (float)q8_quant(v[e + 1], id) * dd);
             packed[e / 2] = *reinterpret_cast<const uint32_t*>(&b);
         }
         uint4* dst = reinterpret_cast<uint4*>(out + (size_t)g * 32);
@@ -139,7 +143,7 @@ __global__ void quant_rows_bf16_kernel(const uint8_t* x, int act_bf16, int rows,
 }
 
 struct TcParams {
-    const __nv_bfloat16* a;  // gate_up: token rows [T][K] (gathered through tokmap/topk); down: position rows [P][K]
+    const __half* a;  // gate_up: token rows [T][K] (gathered through tokmap/topk); down: position rows [P][K]
     const uint8_t* wbase;    // weight records, as GemmParams
     int64_t rec;
     int rows_per_rec, rs, sc_off, ss, nrec, K, N, scale_bf16;
@@ -148,7 +152,7 @@ struct TcParams {
     const int32_t* mtile_start;  // tiles of kTcM rows per expert
     const int32_t* tokmap;
     int topk, E;
-    __nv_bfloat16* ha;  // gate_up output: bf16(q_h * d_h) [P][I]
+    __half* ha;  // gate_up output: fp16(q_h * d_h) [P][I]
     float* out;         // down output: [P][H]
     int32_t* err;
 };
@@ -220,7 +224,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
         // A: 128 rows x 8 chunks of 16 B, chunk c of row r at position c ^ (r & 7)
         for (int ch = tid; ch < kTcM * 8; ch += kTcProducers) {
             const int r = ch >> 3, c = ch & 7;
-            const __nv_bfloat16* src = p.a + s_arow[r] * p.K + (int64_t)ks * kTcK + c * 8;
+            const __half* src = p.a + s_arow[r] * p.K + (int64_t)ks * kTcK + c * 8;
             cp_async16(sA + r * 128 + ((c ^ (r & 7)) << 4), src, r < mrows);
         }
     };
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
         if (0 < nsteps) load_raw(0, rb0);
         if (1 < nsteps) load_raw(1, rb1);
     }
-    const uint32_t idesc = tc_idesc_bf16(kTcM, kTcN);
+    const uint32_t idesc = tc_idesc_f16(kTcM, kTcN);
     const bool sbf = p.scale_bf16 != 0;
     bool ok = true;
     for (int s = 0; s < kStagesTc - 1; ++s) {
@@ -257,7 +261,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
         uint8_t* base = smem + (size_t)st * S::kBytes;
         cp_async_wait<kStagesTc - 2>();
         __syncthreads();
-        {   // dequantise B: thread -> (row tid/2, 32-block tid%2) -> 16 bf16 pairs = 4 chunks
+        {   // dequantise B: thread -> (row tid/2, 32-block tid%2) -> 16 fp16 pairs = 4 chunks
             const int n = tid >> 1, h = tid & 1;
             const RawB cur = rb0;
             rb0 = rb1;
@@ -272,7 +276,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
                     for (int j = 0; j < 8; j += 2) {  // 2^23 + n as float bits, minus 2^23 + 8: exact n - 8
                         const float v0 = (__uint_as_float(((qq[i] >> (4 * j)) & 15u) | 0x4B000000u) - 8388616.0f) * dw;
                         const float v1 = (__uint_as_float(((qq[i] >> (4 * j + 4)) & 15u) | 0x4B000000u) - 8388616.0f) * dw;
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(v0, v1);
+                        const __half2 b2 = __floats2half2_rn(v0, v1);
                         pk[4 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
                     }
             } else {  // word i = elements 4i..4i+3 (int8)
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
                         // byte b ^ 0x80 = q + 128: 2^23 + q + 128 as float bits, minus 2^23 + 128
                         const float v0 = (__uint_as_float((((qq[i] >> (8 * j)) & 0xffu) ^ 0x80u) | 0x4B000000u) - 8388736.0f) * dw;
                         const float v1 = (__uint_as_float((((qq[i] >> (8 * j + 8)) & 0xffu) ^ 0x80u) | 0x4B000000u) - 8388736.0f) * dw;
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(v0, v1);
+                        const __half2 b2 = __floats2half2_rn(v0, v1);
                         pk[2 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
                     }
             }
@@ -351,13 +355,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
                     hv[u] = silu_mul(v[2 * u], v[2 * u + 1]);
                     amax = fmaxf(amax, fabsf(hv[u]));
                 }
+                if (amax > 65504.f) atomicExch(p.err, kErrRange);
                 const float dd = q8_scale(amax);
                 const float id = q8_inv(dd);
                 uint32_t pk[16];
 #pragma unroll
                 for (int u = 0; u < 32; u += 2) {
-                    const __nv_bfloat162 b2 =
-                        __floats2bfloat162_rn((float)q8_quant(hv[u], id) * dd, (float)q8_quant(hv[u + 1], id) * dd);
+                    const __half2 b2 = __floats2half2_rn((float)q8_quant(hv[u], id) * dd, (float)q8_quant(hv[u + 1], id) * dd);
                     pk[u / 2] = *reinterpret_cast<const uint32_t*>(&b2);
                 }
                 uint4* dst = reinterpret_cast<uint4*>(p.ha + (int64_t)pos * I + u0);

@@ -269,3 +269,13 @@ def test_gemm_tile_rows_variants(qt, bm, monkeypatch):
     y, y_ref, _ = run_engine(qt, 32, 1024, 384, 90, 8, seed=7, bad_ids=True)
     rel, cos = parity(y, y_ref)
     assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
+
+
+@pytest.mark.parametrize("scale_bf16,act_bf16", [(True, True), (False, False)])
+@pytest.mark.parametrize("qt", [0, 1])
+def test_tcgen05_gemm_dtypes(qt, scale_bf16, act_bf16, monkeypatch):
+    # the tcgen05 path with bf16 / fp16 block scales and bf16 / fp16 activations
+    monkeypatch.setenv("MOE_GEMM_BM", "128")
+    y, y_ref, _ = run_engine(qt, 16, 1024, 384, 150, 8, seed=13, scale_bf16=scale_bf16, act_bf16=act_bf16)
+    rel, cos = parity(y, y_ref)
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
