@@ -116,7 +116,7 @@ def q8_quantize_torch(w):
     return q.reshape(shp), d32.to(torch.float16)
 
 
-def make_layer(quant, shape, seed, device, e_lo, e_hi, world, rank):
+def make_layer(quant, shape, seed, device, e_lo, e_hi, world, rank, placement=None):
     """A loaded MoEInfer handle with one synthetic layer (BASELINE configs value distributions)."""
     import torch
     H_, I_, E_ = SHAPES[shape]
@@ -126,6 +126,8 @@ def make_layer(quant, shape, seed, device, e_lo, e_hi, world, rank):
         h.set_group_size(128)
     if world > 1:
         h.set_expert_parallel(rank, world)
+        if placement is not None:
+            h.set_expert_placement(placement[rank])
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     if quant == "awq":  # q, z uniform [0,15] (random words), bf16 scales U(0.001, 0.01)
@@ -349,13 +351,6 @@ def run_ours(args):
     bpe = bytes_per_expert(args.quant, H, I)
     el = E // world
     e_lo, e_hi = rank * el, (rank + 1) * el
-    handles = []
-    for s in range(nsets):
-        h = make_layer(args.quant, args.shape, 1000 + s, dev, e_lo, e_hi, world, rank)
-        h.reserve(max(T, 32), K)
-        handles.append(h)
-    torch.cuda.synchronize()
-
     # per-step inputs: hidden + routing
     g = torch.Generator(device=dev)
     g.manual_seed(7)
@@ -366,6 +361,29 @@ def run_ours(args):
         ids, w = make_routing(args.routing, T, E, K, g, dev)
         xs.append(x); idss.append(ids); wss.append(w)
         nbytes.append(int(torch.unique(ids).numel()) * bpe)
+    placement = None
+    if world > 1 and args.placement == "balanced":  # experts dealt to ranks by the routings' load
+        from moe_ascend_opt_b200.ep import balanced_placement
+        load = torch.bincount(torch.cat([i.flatten() for i in idss]).long(), minlength=E).cpu().numpy()
+        placement = balanced_placement(load, world)
+
+    imbalance = None
+    if world > 1:  # max / mean over ranks of the active experts' bytes, averaged over the routings
+        owner = np.zeros(E, np.int64)
+        for r in range(world):
+            owner[placement[r] if placement is not None else list(range(r * el, (r + 1) * el))] = r
+        per_rank = np.zeros(world)
+        for ids in idss:
+            for e in torch.unique(ids).cpu().numpy():
+                per_rank[owner[e]] += bpe
+        imbalance = round(float(per_rank.max() / max(per_rank.mean(), 1e-9)), 3)
+
+    handles = []
+    for s in range(nsets):
+        h = make_layer(args.quant, args.shape, 1000 + s, dev, e_lo, e_hi, world, rank, placement)
+        h.reserve(max(T, 32), K)
+        handles.append(h)
+    torch.cuda.synchronize()
     combine_out = [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(nin)]
 
     # N>1, decode sizes: the partials are summed inside the fused kernel over NVLink peer
@@ -488,6 +506,8 @@ def run_ours(args):
                       "l2": f"inputs larger than L2: {nsets} rotating weight sets x {E} experts "
                             f"({nsets * E * bpe / 1e9:.1f} GB) and {nin} rotating routings",
                       "parallelism": f"ep{world}" if world > 1 else "single",
+                      "placement": args.placement if world > 1 else "n/a",
+                      "rank_load_imbalance": imbalance,
                       "combine": ("in-kernel over NVLink peer memory" if fused else "fp32 partial + NCCL all-reduce")
                       if world > 1 else "in-kernel",
                       "launch": (f"cuda_graph ({ncycle} layer steps per graph replay)" if cycle_graph is not None
@@ -614,6 +634,8 @@ def main():
     ap.add_argument("--sweep-tokens", default="1,4,8,32,128,1024,4096")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock soak (profiling runs)")
     ap.add_argument("--nccl-combine", action="store_true", help="N>1: fp32 partial + NCCL all-reduce at every T")
+    ap.add_argument("--placement", default="contiguous", choices=["contiguous", "balanced"],
+                    help="N>1: experts per rank in contiguous blocks or dealt by routing load")
     ap.add_argument("--cpu-worker", type=float, default=None)
     args = ap.parse_args()
     if args.cpu_worker is not None:

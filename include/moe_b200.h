@@ -177,6 +177,14 @@ int moe_engine_p2p_connect(moe_engine* eng, int32_t rank, int32_t world, const v
 int moe_engine_p2p_enable(moe_engine* eng, int32_t on);
 int moe_engine_p2p_covers(moe_engine* eng, int64_t num_tokens);
 
+/* Expert placement for load balance under skewed routing (the reference places experts
+ * on NUMA nodes in contiguous blocks, moe_infer.cpp:143-205).  Replaces the contiguous block
+ * [expert_offset, expert_offset + num_experts) by an explicit map: local_of_global[g] is
+ * the local index (0 .. num_experts-1) of global expert g on this engine, or -1 when another
+ * engine holds it; every local index appears once.  The weights loaded into local slot l
+ * must be those of the global expert mapped to l.  Copied to the device (synchronises). */
+int moe_engine_set_expert_map(moe_engine* eng, const int32_t* local_of_global, int64_t num_global);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,6 +23,7 @@ SYMBOLS = [
     "moe_engine_device_error", "moe_engine_export_expert", "moe_route_topk", "moe_route_permute",
     "moe_quantize_rows_q8_0", "moe_engine_debug_timeline", "moe_engine_forward_noalloc", "moe_last_error",
     "moe_engine_p2p_mailbox", "moe_engine_p2p_connect", "moe_engine_p2p_enable", "moe_engine_p2p_covers",
+    "moe_engine_set_expert_map",
 ]
 
 
@@ -71,6 +72,7 @@ def lib() -> C.CDLL:
             "moe_engine_p2p_connect": [_P, _I32, _I32, _P],
             "moe_engine_p2p_enable": [_P, _I32],
             "moe_engine_p2p_covers": [_P, _I64],
+            "moe_engine_set_expert_map": [_P, _P, _I64],
         }
         for name, args in sig.items():
             f = getattr(L, name)

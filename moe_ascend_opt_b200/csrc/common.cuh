@@ -18,6 +18,15 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 enum ErrCode : int32_t { kErrNone = 0, kErrGridBarrier = 1, kErrFullWait = 2, kErrEmptyWait = 3, kErrPeerWait = 4,
                          kErrRange = 5 };
 
+// Global expert id -> this engine's local id, or -1 for experts it does not hold: through
+// the placement map when one is set (local_of_global[gid]), else the contiguous block
+// [e_off, e_off + E).  Invalid ids are skipped like in the reference (moe_common.cpp:158).
+MOE_DEV int local_expert(int gid, int e_off, int E, const int32_t* emap, int emap_n) {
+    if (emap) return (gid >= 0 && gid < emap_n) ? emap[gid] : -1;
+    const int g = gid - e_off;
+    return (g >= 0 && g < E) ? g : -1;
+}
+
 MOE_DEV float act_to_f32(const void* p, int64_t i, int is_bf16) {
     if (is_bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
     return __half2float(reinterpret_cast<const __half*>(p)[i]);

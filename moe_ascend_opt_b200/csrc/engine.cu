@@ -56,6 +56,8 @@ struct moe_engine {
     // down weights re-laid for the split-K decode kernel (Q8_0 / Q4_0): [E][I/32][H/32] slices
     uint8_t* dk = nullptr;
     bool use_sk = true;  // decode through moe_decode_sk_kernel when the layout allows
+    int32_t* emap = nullptr;  // optional placement map: global expert id -> local id or -1
+    int32_t emap_n = 0;
     int32_t sk_cost_a = 3;  // its chunk cost model: streaming share per chunk vs one token of compute
     int32_t sk_min_chunks_per_cta = 2;  // use it from this many (unique expert x I/32) chunks per CTA
     // expert-parallel combine over peer memory (moe_engine_p2p_mailbox / _connect)
@@ -509,6 +511,7 @@ bool plan_decode_sk(const moe_engine* eng, int T, int K, DecodePlan& pl) {
     if (off > eng->max_smem - 256) return false;
     p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
     p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
+    p.emap = eng->emap; p.emap_n = eng->emap_n;
     p.scale_bf16 = eng->scale_bf16;
     p.group = eng->cfg.group_size;
     p.flags = eng->decode_flags;
@@ -559,6 +562,7 @@ bool plan_decode_lpr(const moe_engine* eng, int T, int K, int lpr0, DecodePlan& 
     if (off > eng->max_smem - 256) return false;
     p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
     p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
+    p.emap = eng->emap; p.emap_n = eng->emap_n;
     p.scale_bf16 = eng->scale_bf16;
     p.group = eng->cfg.group_size;
     p.flags = eng->decode_flags;
@@ -807,10 +811,11 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     if (int rc = gemm_workspace(eng, T, K, w)) return rc;
     const int nblk = (TK + gemm::kChunk - 1) / gemm::kChunk;
     const int eoff = eng->cfg.expert_offset;
-    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk);
+    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk);
     gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
                                                                                   w.mtile, std::abs(gemm_tile_rows(eng, TK)));
-    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, w.blk, w.starts, w.smap, w.tokmap);
+    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk, w.starts,
+                                                       w.smap, w.tokmap);
     const int bm = gemm_tile_rows(eng, TK);
     if (bm == 128) {
         if (int rc = launch_gemms_tc<Q4>(eng, w, x, act_bf16, T, K, st)) return rc;
@@ -918,6 +923,7 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     cudaFree(eng->gu);
     cudaFree(eng->dn);
     cudaFree(eng->dk);
+    cudaFree(eng->emap);
     cudaFree(eng->part);
     for (int q = 0; q < kMaxPeers; ++q)
         if (eng->peer_base[q]) cudaIpcCloseMemHandle(eng->peer_base[q]);
@@ -1425,5 +1431,26 @@ extern "C" int moe_engine_p2p_enable(moe_engine* eng, int32_t on) {
     if (int rc = check_engine(eng)) return rc;
     if (on && eng->p2p_world < 2) return fail(MOE_ERR_STATE, "not connected (moe_engine_p2p_connect)");
     eng->p2p_active = on != 0;
+    return MOE_OK;
+}
+
+// =================================================================== expert placement
+extern "C" int moe_engine_set_expert_map(moe_engine* eng, const int32_t* local_of_global, int64_t num_global) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!local_of_global || num_global <= 0 || num_global > (1 << 20)) return fail(MOE_ERR_INVALID, "bad expert map");
+    const int64_t E = eng->cfg.num_experts;
+    std::vector<int> seen(E, 0);
+    for (int64_t g = 0; g < num_global; ++g) {
+        const int32_t l = local_of_global[g];
+        if (l == -1) continue;
+        if (l < 0 || l >= E || seen[l]++) return fail(MOE_ERR_INVALID, "expert map must send each local expert id once");
+    }
+    DeviceGuard g(eng->cfg.device);
+    CUDA_TRY(cudaDeviceSynchronize());  // the old map may still be read by queued work
+    if (eng->emap) CUDA_TRY(cudaFree(eng->emap));
+    eng->emap = nullptr;
+    CUDA_TRY(cudaMalloc(&eng->emap, (size_t)num_global * sizeof(int32_t)));
+    CUDA_TRY(cudaMemcpy(eng->emap, local_of_global, (size_t)num_global * sizeof(int32_t), cudaMemcpyHostToDevice));
+    eng->emap_n = (int32_t)num_global;
     return MOE_OK;
 }

@@ -61,6 +61,8 @@ struct DecodeParams {
     const uint8_t* dn;
     int32_t rs1, ss1, rs2, ss2;
     int32_t E, e_off, H, I, T, K;
+    const int32_t* emap;  // optional placement map: global expert id -> local id or -1 [emap_n]
+    int32_t emap_n;
     int32_t scale_bf16, act_bf16, out_kind;  // out_kind: 0 f16, 1 bf16, 2 f32
     const void* x;
     void* y;
@@ -179,15 +181,15 @@ MOE_DEV RouteSmem carve_route(int32_t* base, int TK, int E) {
 // Stable counting sort by one warp (moe_common.cpp:146-184): pairs are taken in
 // (t,k) order 32 at a time; lanes with the same expert rank themselves with
 // __match_any_sync, so positions inside an expert follow pair order exactly.
-MOE_DEV void route_warp(const int32_t* g_ids, int TK, int E, int e_off, RouteSmem r, int lane) {
+MOE_DEV void route_warp(const int32_t* g_ids, int TK, int E, int e_off, const int32_t* emap, int emap_n, RouteSmem r,
+                        int lane) {
     for (int e = lane; e < E; e += 32) r.cnt[e] = 0;
     __syncwarp();
     for (int i0 = 0; i0 < TK; i0 += 32) {
         const int i = i0 + lane;
         int e = -1;
         if (i < TK) {
-            const int g = g_ids[i] - e_off;
-            e = (g >= 0 && g < E) ? g : -1;
+            e = local_expert(g_ids[i], e_off, E, emap, emap_n);
             r.ids[i] = e;
         }
         const unsigned peers = __match_any_sync(0xffffffffu, e);
@@ -618,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     if (warp == kWarps - 1) {  // one warp routes while the others quantise the tokens
         // this launch's barrier target: the load is in flight while the warp routes
         const unsigned long long launch_idx = barrier_launch_index(p.bar, (uint32_t)G);
-        route_warp(p.ids, TK, E, p.e_off, rt, lane);
+        route_warp(p.ids, TK, E, p.e_off, p.emap, p.emap_n, rt, lane);
         if (lane == 0) {
             s_ok = 1;
             s_launch = launch_idx;

@@ -46,6 +46,7 @@ struct MoEInferHandle : torch::CustomClassHolder {
     int64_t quant_type;
     int64_t group_size = 128;
     int64_t ep_rank = 0, ep_size = 1;
+    std::vector<int64_t> placement;  // global ids of the experts held here, in local order (empty: contiguous block)
     moe_engine* eng = nullptr;
     int device = -1;
 
@@ -58,8 +59,24 @@ struct MoEInferHandle : torch::CustomClassHolder {
         if (eng) moe_engine_destroy(eng);
     }
 
-    int64_t local_experts() const { return E / ep_size; }
-    int64_t expert_offset() const { return ep_rank * local_experts(); }
+    int64_t local_experts() const { return placement.empty() ? E / ep_size : (int64_t)placement.size(); }
+    int64_t expert_offset() const { return placement.empty() ? ep_rank * local_experts() : 0; }
+    int64_t local_of(int64_t e) const {  // -1: another rank's expert
+        if (placement.empty()) return (e >= expert_offset() && e < expert_offset() + local_experts()) ? e - expert_offset() : -1;
+        for (size_t l = 0; l < placement.size(); ++l)
+            if (placement[l] == e) return (int64_t)l;
+        return -1;
+    }
+    void set_expert_placement(const std::vector<int64_t>& experts) {
+        TORCH_CHECK(!eng, "set_expert_placement must precede weight loading");
+        TORCH_CHECK(!experts.empty(), "empty placement");
+        std::vector<char> seen(E, 0);
+        for (int64_t e : experts) {
+            TORCH_CHECK(e >= 0 && e < E && !seen[e], "placement: expert ids must be distinct and in [0, E)");
+            seen[e] = 1;
+        }
+        placement = experts;
+    }
 
     void set_expert_parallel(int64_t rank, int64_t size) {
         TORCH_CHECK(!eng, "set_expert_parallel must precede weight loading");
@@ -84,11 +101,20 @@ struct MoEInferHandle : torch::CustomClassHolder {
         cfg.device = device;
         cfg.expert_offset = (int32_t)expert_offset();
         check_rc(moe_engine_create(&cfg, &eng), "moe_engine_create");
+        if (!placement.empty()) {
+            std::vector<int32_t> m(E, -1);
+            for (size_t l = 0; l < placement.size(); ++l) m[placement[l]] = (int32_t)l;
+            check_rc(moe_engine_set_expert_map(eng, m.data(), E), "set_expert_placement");
+        }
     }
 
     // slice the local experts of a full [E, ...] tensor and make it contiguous
     at::Tensor local(const at::Tensor& t) const {
         TORCH_CHECK(t.dim() == 3 && t.size(0) == E, "E mismatch");
+        if (!placement.empty()) {
+            auto idx = at::tensor(placement, at::TensorOptions().dtype(at::kLong)).to(t.device());
+            return t.index_select(0, idx).contiguous();
+        }
         if (ep_size == 1) return t.contiguous();
         return t.narrow(0, expert_offset(), local_experts()).contiguous();
     }
@@ -150,11 +176,12 @@ struct MoEInferHandle : torch::CustomClassHolder {
             TORCH_CHECK(w.size(0) == H && w.size(1) == I, "down weight must be [H,I]");
         }
         TORCH_CHECK(e >= 0 && e < E, "expert index out of range");
-        if (e < expert_offset() || e >= expert_offset() + local_experts()) return;  // another rank's expert
+        const int64_t le = local_of(e);
+        if (le < 0) return;  // another rank's expert
         ensure_engine();
         c10::cuda::CUDAGuard g(device);
         auto wc = w.contiguous();
-        check_rc(moe_engine_quantize_store_expert(eng, e - expert_offset(), p, wc.data_ptr(), dtype_code(wc.scalar_type()),
+        check_rc(moe_engine_quantize_store_expert(eng, le, p, wc.data_ptr(), dtype_code(wc.scalar_type()),
                                                   wc.is_cuda() ? 1 : 0, cur_stream(device)),
                  "quantize_and_store_expert");
     }
@@ -319,6 +346,7 @@ TORCH_LIBRARY(nanovllm, m) {
         .def("store_quantized_repack", &MoEInferHandle::store_quantized_repack)
         .def("store_awq", &MoEInferHandle::store_awq)
         .def("set_expert_parallel", &MoEInferHandle::set_expert_parallel)
+        .def("set_expert_placement", &MoEInferHandle::set_expert_placement)
         .def("set_group_size", &MoEInferHandle::set_group_size)
         .def("p2p_mailbox", &MoEInferHandle::p2p_mailbox)
         .def("p2p_connect", &MoEInferHandle::p2p_connect)

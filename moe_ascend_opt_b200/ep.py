@@ -1,7 +1,8 @@
 """Expert parallelism across the GPUs of one node (one process per GPU).
 
-Experts are placed in contiguous blocks: rank r of W holds global experts
-[r*E/W, (r+1)*E/W).  Every rank receives the full hidden states and routing
+Experts are placed in contiguous blocks by default: rank r of W holds global experts
+[r*E/W, (r+1)*E/W); `balanced_placement` deals them by routing load instead (skewed,
+e.g. Zipf, routing), and the kernels then map ids through a per-rank table.  Every rank receives the full hidden states and routing
 (as in the reference's caller, which hands the same [T,H] to the engine), runs
 the fused layer over its local experts only -- ids outside the block are
 skipped exactly like invalid ids in the reference (moe_common.cpp:158,175-181)
@@ -28,6 +29,43 @@ def expert_partition(num_experts: int, world: int) -> List[Tuple[int, int]]:
     return [(r * per, (r + 1) * per) for r in range(world)]
 
 
+def balanced_placement(load, world: int) -> List[List[int]]:
+    """Experts -> ranks from routing statistics (tokens per expert, e.g. counted over a
+    calibration batch): every rank keeps E/W experts (equal weight memory), and the
+    experts are dealt heaviest first to the rank with the least load that still has room,
+    so Zipf-skewed routing no longer piles the hot experts onto one rank."""
+    load = np.asarray(load, np.float64)
+    E = load.shape[0]
+    if world < 1 or E % world != 0:
+        raise ValueError(f"num_experts={E} must be divisible by the world size {world}")
+    per = E // world
+    ranks: List[List[int]] = [[] for _ in range(world)]
+    tot = np.zeros(world)
+    for e in np.argsort(-load, kind="stable"):
+        open_r = [r for r in range(world) if len(ranks[r]) < per]
+        r = min(open_r, key=lambda q: (tot[q], q))
+        ranks[r].append(int(e))
+        tot[r] += load[e]
+    return [sorted(r) for r in ranks]
+
+
+def placement_imbalance(load, placement: List[List[int]]) -> float:
+    """max / mean of the per-rank load (1.0 = perfectly balanced)."""
+    load = np.asarray(load, np.float64)
+    per_rank = np.array([load[r].sum() for r in placement])
+    return float(per_rank.max() / max(per_rank.mean(), 1e-12))
+
+
+def local_ids_map(ids: np.ndarray, experts: List[int]) -> np.ndarray:
+    """Global ids -> local ids of a rank holding `experts` (in local order), -1 elsewhere."""
+    m = np.full(max(experts) + 1, -1, np.int32)
+    for l, e in enumerate(experts):
+        m[e] = l
+    ids = np.asarray(ids, np.int64)
+    ok = (ids >= 0) & (ids < m.size)
+    return np.where(ok, m[np.clip(ids, 0, m.size - 1)], -1).astype(np.int32)
+
+
 def local_ids(ids: np.ndarray, lo: int, hi: int) -> np.ndarray:
     """Global ids -> this rank's local ids, -1 for experts held elsewhere (the kernel's remap)."""
     ids = np.asarray(ids, np.int32)
@@ -42,7 +80,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, num_experts: int, hidden: int, inter: int, quant_type: int, group=None,
-                 group_size: int = 128):
+                 group_size: int = 128, placement: Optional[List[List[int]]] = None):
         import torch
         import torch.distributed as dist
 
@@ -56,6 +94,10 @@ class ExpertParallelMoE:
         if quant_type == 2:
             self.handle.set_group_size(group_size)
         self.handle.set_expert_parallel(self.rank, self.world)
+        if placement is not None:  # e.g. balanced_placement(tokens per expert, world)
+            if len(placement) != self.world:
+                raise ValueError("placement needs one expert list per rank")
+            self.handle.set_expert_placement(list(placement[self.rank]))
 
     def load_quantized(self, gate_up_qs, gate_up_d, down_qs, down_d):
         self.handle.store_quantized_repack(gate_up_qs, gate_up_d, down_qs, down_d)

@@ -122,3 +122,30 @@ def test_expert_parallel_partials_on_one_gpu():
     y = (parts[0] + parts[1]).cpu().numpy()
     rel, cos = parity(y, O.moe_forward_q(1, False, xf, ids, w, gq, gd, dq, dd))
     assert rel <= 2e-3 and cos >= MIN_COS, (rel, cos)
+
+
+@pytest.mark.parametrize("T", [1, 40])  # decode kernel / grouped GEMMs
+def test_expert_placement_partials_on_one_gpu(T):
+    """Two engines with interleaved (non-contiguous) expert sets sum to the full layer."""
+    import moe_ascend_opt_b200  # noqa: F401
+    from oracle import oracle as O
+    from tests.helpers import q_weights, tokens
+    E, H, I, K = 32, 1024, 384, 8
+    gq, gd, dq, dd = q_weights(1, E, H, I, 23)
+    xb, xf, ids, w = tokens(T, H, E, K, 23)
+    placement = [list(range(0, E, 2)), list(range(1, E, 2))]
+    x = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+    total = None
+    for r in range(2):
+        h = torch.classes.nanovllm.MoEInfer(E, H, I, 1)
+        h.set_expert_parallel(r, 2)
+        h.set_expert_placement(placement[r])
+        h.store_quantized_repack(torch.from_numpy(gq), torch.from_numpy(gd.view(np.int16)).view(torch.float16),
+                                 torch.from_numpy(dq), torch.from_numpy(dd.view(np.int16)).view(torch.float16))
+        part = torch.ops.nanovllm.moe_forward_partial(x, torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), h)
+        torch.cuda.synchronize()
+        assert h.device_error() == 0
+        total = part if total is None else total + part
+    y_ref = O.moe_forward_q(1, False, xf, ids, w, gq, gd, dq, dd)
+    rel = float(np.abs(total.cpu().numpy() - y_ref).max() / np.abs(y_ref).max())
+    assert rel <= 1e-2, rel
