@@ -527,20 +527,32 @@ def run_ours(args):
                                       "grouped_gemm_wm_kernel" if T * K <= 24 * E else "grouped_gemm_kernel")}
     # end-to-end through the public op with host buffers and copies in the timed region
     if rank == 0 or world > 1:
-        xh = [x.cpu().pin_memory() for x in xs]
-        ih = [i.cpu().pin_memory() for i in idss]
-        wh = [w.cpu().pin_memory() for w in wss]
+        # one pinned host buffer per step holding hidden | topk_ids | topk_w (16-byte aligned
+        # fields), one H2D copy into the matching device buffer, views as the op's inputs
+        a16 = lambda n: (n + 15) // 16 * 16
+        nbx, nbi = T * H * 2, T * K * 4
+        off_i = a16(nbx)
+        off_w = a16(off_i + nbi)
+        tot = a16(off_w + nbi)
+        hbuf = []
+        for j in range(nin):
+            b = torch.empty(tot, dtype=torch.uint8).pin_memory()
+            b[:nbx].copy_(xs[j].cpu().contiguous().view(torch.uint8).flatten())
+            b[off_i:off_i + nbi].copy_(idss[j].cpu().contiguous().view(torch.uint8).flatten())
+            b[off_w:off_w + nbi].copy_(wss[j].cpu().contiguous().view(torch.uint8).flatten())
+            hbuf.append(b)
+        dbuf = torch.empty(tot, dtype=torch.uint8, device=dev)
+        xd = dbuf[:nbx].view(torch.bfloat16).view(T, H)
+        idd = dbuf[off_i:off_i + nbi].view(torch.int32).view(T, K)
+        wd = dbuf[off_w:off_w + nbi].view(torch.float32).view(T, K)
         yh = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
-        xd = torch.empty_like(xs[0]); idd = torch.empty_like(idss[0]); wd = torch.empty_like(wss[0])
         n_e2e = min(args.steps, 2000)
 
         def e2e_step(i):
             j = i % nin
-            xd.copy_(xh[j], non_blocking=True)
-            idd.copy_(ih[j], non_blocking=True)
-            wd.copy_(wh[j], non_blocking=True)
+            dbuf.copy_(hbuf[j], non_blocking=True)
             h = handles[i % nsets]
-            if world == 1:
+            if world == 1 or fused:
                 y = torch.ops.nanovllm.moe_forward(xd, idd, wd, h)
             else:
                 y = torch.ops.nanovllm.moe_forward_partial(xd, idd, wd, h)
@@ -548,28 +560,77 @@ def run_ours(args):
                 y = y.to(torch.bfloat16)
             yh.copy_(y, non_blocking=True)
 
-        for i in range(3):
-            e2e_step(i)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(n_e2e):
-            e2e_step(i)
-        e1.record()
-        torch.cuda.synchronize()
-        ems = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ems], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
+        # graph mode, as a serving loop runs it: per step one CUDA graph holding the H2D copy
+        # from that step's pinned buffer, the reference's graph-capture op
+        # (moe_forward_npu_graph_out with a MoEGraphContext) and the D2H copy of the output
+        e2e_graphs = None
+        if (world == 1 or fused) and not args.no_graph:
+            try:
+                ctxs = [torch.classes.nanovllm.MoEGraphContext(h, T, K, 1) for h in handles]
+                ydev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+                nstep_g = int(np.lcm(nsets, nin))
+
+                def g_step(i):
+                    dbuf.copy_(hbuf[i % nin], non_blocking=True)
+                    torch.ops.nanovllm.moe_forward_npu_graph_out(xd, idd, wd, handles[i % nsets], ctxs[i % nsets], ydev)
+                    yh.copy_(ydev, non_blocking=True)
+
+                sg = torch.cuda.Stream()
+                sg.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(sg):
+                    for i in range(3):
+                        g_step(i)
+                torch.cuda.current_stream().wait_stream(sg)
+                torch.cuda.synchronize()
+                e2e_graphs = []
+                for i in range(nstep_g):
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr):
+                        g_step(i)
+                    e2e_graphs.append(gr)
+                torch.cuda.synchronize()
+            except Exception as ex:
+                print(f"[bench] e2e graph capture unavailable ({str(ex)[:80]})", file=sys.stderr)
+                e2e_graphs = None
+
+        def time_e2e(fn):
+            for i in range(3):
+                fn(i)
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(n_e2e):
+                fn(i)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            return ms
+
         eb = sum(nbytes[i % nin] for i in range(n_e2e)) / n_e2e
-        out["e2e"] = {"value": round(eb / (ems / n_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
-                      "ms_per_step": round(ems / n_e2e, 6), "steps": n_e2e,
-                      "h2d_bytes_per_step": T * H * 2 + T * K * 8, "d2h_bytes_per_step": T * H * 2,
-                      "api": "torch.ops.nanovllm.moe_forward (eager, pinned host buffers)"}
+        ems_eager = time_e2e(e2e_step)
+        eager = {"value": round(eb / (ems_eager / n_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                 "ms_per_step": round(ems_eager / n_e2e, 6), "steps": n_e2e,
+                 "h2d_bytes_per_step": tot, "d2h_bytes_per_step": T * H * 2,
+                 "api": "torch.ops.nanovllm.moe_forward (eager; one pinned H2D copy of hidden, "
+                        "ids and weights, one D2H copy of the output)"}
+        if e2e_graphs is not None:
+            ems = time_e2e(lambda i: e2e_graphs[i % len(e2e_graphs)].replay())
+            out["e2e"] = {"value": round(eb / (ems / n_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                          "ms_per_step": round(ems / n_e2e, 6), "steps": n_e2e,
+                          "h2d_bytes_per_step": tot, "d2h_bytes_per_step": T * H * 2,
+                          "api": "torch.ops.nanovllm.moe_forward_npu_graph_out + MoEGraphContext, one CUDA "
+                                 "graph per step with the pinned H2D copy of hidden/ids/weights and the D2H "
+                                 "copy of the output"}
+            out["e2e_eager"] = eager
+        else:
+            out["e2e"] = eager
     if world == 1 and not args.no_cpu and default_wl:
         out["cpu_baseline"] = cpu_baseline(T)
     if args.sweep and world == 1:

@@ -347,6 +347,11 @@ TORCH_LIBRARY(nanovllm, m) {
         .def("store_awq", &MoEInferHandle::store_awq)
         .def("set_expert_parallel", &MoEInferHandle::set_expert_parallel)
         .def("set_expert_placement", &MoEInferHandle::set_expert_placement)
+        .def("engine_handle",  // the moe_engine* behind this handle, for direct C-ABI calls (include/moe_b200.h)
+             [](const c10::intrusive_ptr<MoEInferHandle>& s) -> int64_t {
+                 TORCH_CHECK(s->eng, "no weights loaded");
+                 return (int64_t)reinterpret_cast<intptr_t>(s->eng);
+             })
         .def("set_group_size", &MoEInferHandle::set_group_size)
         .def("p2p_mailbox", &MoEInferHandle::p2p_mailbox)
         .def("p2p_connect", &MoEInferHandle::p2p_connect)
