@@ -78,7 +78,8 @@ struct moe_engine {
     int64_t gemm_min_tokens = 8;  // forwards with more tokens take the grouped-GEMM path
     int32_t decode_flags = kFlagEvictFirst;
     int32_t gemm_bm = 0;  // grouped-GEMM tile kind (gemm_tile_rows codes); 0 = by tokens per expert
-    int64_t tc_min_per_expert = 48;  // tcgen05 bf16 GEMMs from this many expected tokens per expert
+    int64_t tc_min_per_expert = 48;  // tcgen05 GEMMs from this many expected tokens per expert
+    int64_t awq_gemm_min_tokens = 24;  // AWQ: the tcgen05 GEMMs for calls with more tokens
     int32_t dist_min_blocks = -1;  // decode: requantise h before the barrier from this many blocks (-1: 2 x SMs)
     // grouped-GEMM path workspace (one allocation, carved per call)
     uint8_t* gws = nullptr;
@@ -696,23 +697,27 @@ int gemm_tile_rows(const moe_engine* eng, int64_t TK) {
     return per_expert <= 6 ? -8 : (per_expert <= 24 ? -16 : (per_expert <= 40 ? 32 : 64));
 }
 
-template <bool Q4>
+// The tcgen05 grouped GEMMs of one layer.  WF: 0 Q8_0, 1 Q4_0 (A = fp16(q_a d_a) rows from
+// quant_rows_f16_kernel), 2 AWQ (A = the 16-bit hidden rows themselves, W4A16).
+template <int WF>
 int launch_gemms_tc(moe_engine* eng, const GemmWs& w, const void* x, int act_bf16, int64_t T, int64_t K,
                     cudaStream_t st) {
     const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
     const int64_t TK = T * K;
-    {
+    const __half* a1 = static_cast<const __half*>(x);  // AWQ: the caller's rows (bf16 or fp16 bits)
+    if (WF != 2) {
         const int nb = (int)(T * (H / 32));
         gemm::quant_rows_f16_kernel<<<std::min((nb + 255) / 256, eng->num_sms * 8), 256, 0, st>>>(
             static_cast<const uint8_t*>(x), act_bf16, (int)T, H, w.xa, eng->err);
         CUDA_TRY(cudaGetLastError());
+        a1 = w.xa;
     }
-    const int smem = gemm::kStagesTc * gemm::StageTc<Q4>::kBytes + 1024;
+    const int smem = gemm::kStagesTc * gemm::StageTc<WF != 0>::kBytes + 1024;
     static thread_local int smem_set[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    auto k1 = gemm::grouped_gemm_tc_kernel<Q4, true>;
-    auto k2 = gemm::grouped_gemm_tc_kernel<Q4, false>;
+    auto k1 = gemm::grouped_gemm_tc_kernel<WF, true>;
+    auto k2 = gemm::grouped_gemm_tc_kernel<WF, false>;
     if (dev < 64 && smem_set[1][dev] < smem) {
         CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         smem_set[1][dev] = smem;
@@ -731,21 +736,54 @@ int launch_gemms_tc(moe_engine* eng, const GemmWs& w, const void* x, int act_bf1
     tp.topk = (int)K;
     tp.E = E;
     tp.err = eng->err;
+    tp.group = eng->cfg.group_size;
+    tp.bf16ops = (WF == 2 && act_bf16) ? 1 : 0;
     gemm::TcParams t1 = tp;  // gate_up: A = token rows, B = unit records (2 rows each)
-    t1.a = w.xa;
+    t1.a = a1;
     t1.wbase = eng->gu; t1.rec = eng->unit_bytes(); t1.rows_per_rec = 2; t1.rs = eng->rs1;
     t1.sc_off = 2 * eng->rs1; t1.ss = eng->ss1; t1.nrec = I; t1.K = H; t1.N = 2 * I;
+    t1.ngk = H / std::max(1, tp.group);
     t1.ha = w.ha;
     k1<<<(unsigned)(mt_bound * (2 * I / gemm::kTcN)), gemm::kTcThreads, smem, st>>>(t1);
     CUDA_TRY(cudaGetLastError());
-    gemm::TcParams t2 = tp;  // down: A = bf16 h rows, B = down row records
+    gemm::TcParams t2 = tp;  // down: A = h rows, B = down row records
     t2.a = w.ha;
     t2.wbase = eng->dn; t2.rec = eng->row_bytes(); t2.rows_per_rec = 1; t2.rs = eng->rs2;
     t2.sc_off = eng->rs2; t2.ss = eng->ss2; t2.nrec = H; t2.K = I; t2.N = H;
+    t2.ngk = I / std::max(1, tp.group);
     t2.out = w.out;
     k2<<<(unsigned)(mt_bound * (H / gemm::kTcN)), gemm::kTcThreads, smem, st>>>(t2);
     CUDA_TRY(cudaGetLastError());
     return MOE_OK;
+}
+
+// AWQ (W4A16) layers with many tokens: routing, the tcgen05 GEMMs on the 16-bit hidden rows,
+// combine.  The per-expert tiles hold 128 tokens, so this pays off from ~24 tokens per call.
+int forward_gemm_awq(moe_engine* eng, const void* x, void* y, const int32_t* ids, const float* tw, int64_t T,
+                     int64_t K, int act_bf16, int out_kind, cudaStream_t st) {
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size;
+    const int TK = (int)(T * K);
+    GemmWs w;
+    if (int rc = gemm_workspace(eng, T, K, w)) return rc;
+    const int nblk = (TK + gemm::kChunk - 1) / gemm::kChunk;
+    const int eoff = eng->cfg.expert_offset;
+    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk);
+    gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
+                                                                                  w.mtile, gemm::kTcM);
+    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk, w.starts,
+                                                       w.smap, w.tokmap);
+    CUDA_TRY(cudaGetLastError());
+    if (int rc = launch_gemms_tc<2>(eng, w, x, act_bf16, T, K, st)) return rc;
+    const int64_t total = T * (H / 4);
+    gemm::combine_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, eng->num_sms * 16), 256, 0, st>>>(
+        w.out, w.smap, tw, (int)T, (int)K, H, y, out_kind);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+bool awq_gemm_ok(const moe_engine* eng) {
+    const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    return eng->cfg.quant_type == MOE_AWQ && H % 128 == 0 && I % 128 == 0 && eng->cfg.num_experts <= 1024;
 }
 
 template <bool Q4, int BT>
@@ -818,7 +856,7 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
                                                        w.smap, w.tokmap);
     const int bm = gemm_tile_rows(eng, TK);
     if (bm == 128) {
-        if (int rc = launch_gemms_tc<Q4>(eng, w, x, act_bf16, T, K, st)) return rc;
+        if (int rc = launch_gemms_tc<Q4 ? 1 : 0>(eng, w, x, act_bf16, T, K, st)) return rc;
     } else {
     {
         const int nb = (int)(T * (H / 32));
@@ -894,6 +932,7 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (const char* v = std::getenv("MOE_DIST_REQUANT_MIN")) eng->dist_min_blocks = std::atoi(v);
     if (const char* v = std::getenv("MOE_DECODE_FLAGS")) eng->decode_flags = std::atoi(v);
     if (const char* v = std::getenv("MOE_TC_MIN_PER_EXPERT")) eng->tc_min_per_expert = std::atoll(v);
+    if (const char* v = std::getenv("MOE_AWQ_GEMM_MIN_TOKENS")) eng->awq_gemm_min_tokens = std::atoll(v);
     if (const char* v = std::getenv("MOE_GEMM_BM")) {  // "w8" / "w16" weights-on-M, "16" / "32" / "64"
         const bool wm = v[0] == 'w';
         const int bm = std::atoi(wm ? v + 1 : v);
@@ -1065,7 +1104,8 @@ extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t t
     if (int rc = check_engine(eng)) return rc;
     if (max_tokens < 0 || top_k <= 0) return fail(MOE_ERR_INVALID, "bad reserve size");
     DeviceGuard g(eng->cfg.device);
-    if (max_tokens > eng->gemm_min_tokens && gemm_path_ok(eng)) {  // the grouped-GEMM path's workspace
+    if ((max_tokens > eng->gemm_min_tokens && gemm_path_ok(eng)) ||
+        (max_tokens > eng->awq_gemm_min_tokens && awq_gemm_ok(eng))) {  // the grouped-GEMM path's workspace
         GemmWs w;
         if (int rc = gemm_workspace(eng, max_tokens, top_k, w)) return rc;
     }
@@ -1106,6 +1146,19 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
     if (eng->p2p_active && !moe_engine_p2p_covers(eng, T))
         return fail(MOE_ERR_STATE, "peer combine covers decode-size calls only; use the fp32 partial and an all-reduce");
+    if (T > eng->awq_gemm_min_tokens && awq_gemm_ok(eng)) {  // AWQ: the tcgen05 GEMMs on the 16-bit rows
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        CUDA_TRY(cudaStreamIsCapturing(st, &cap));
+        const bool timed = cap == cudaStreamCaptureStatusNone;
+        if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
+        const int okind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+        if (int rc = forward_gemm_awq(eng, x, y, topk_ids, topk_w, T, K, act_dtype == MOE_BF16, okind, st)) return rc;
+        if (timed) {
+            CUDA_TRY(cudaEventRecord(eng->ev1, st));
+            eng->timed = true;
+        }
+        return MOE_OK;
+    }
     if (T > eng->gemm_min_tokens && gemm_path_ok(eng)) {  // dense enough for the grouped GEMMs
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
         CUDA_TRY(cudaStreamIsCapturing(st, &cap));
@@ -1384,7 +1437,8 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
 // =================================================================== peer combine (expert parallel)
 extern "C" int moe_engine_p2p_covers(moe_engine* eng, int64_t num_tokens) {
     if (!eng) return 0;
-    return !(num_tokens > eng->gemm_min_tokens && gemm_path_ok(eng)) && num_tokens <= std::max<int64_t>(eng->p2p_tcap, 8);
+    return !(num_tokens > eng->gemm_min_tokens && gemm_path_ok(eng)) &&
+           !(num_tokens > eng->awq_gemm_min_tokens && awq_gemm_ok(eng)) && num_tokens <= std::max<int64_t>(eng->p2p_tcap, 8);
 }
 
 extern "C" int moe_engine_p2p_mailbox(moe_engine* eng, int32_t world, int64_t max_tokens, void* ipc_handle_out) {

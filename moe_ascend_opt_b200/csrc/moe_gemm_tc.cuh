@@ -42,11 +42,11 @@ namespace gemm {
 constexpr int kTcM = 128, kTcN = 128, kTcK = 64;  // tile rows (tokens), cols (weight rows), K step
 constexpr int kStagesTc = 2;  // x 32 KB: with 1 KB alignment slack and 80 registers, 3 CTAs per SM
 
-template <bool Q4>
+template <bool NIB>  // NIB: 4-bit weights (Q4_0, AWQ)
 struct StageTc {
     static constexpr int kA = kTcM * 128;                // fp16 A tile, 128 B per row (SW128 K-major)
     static constexpr int kB = kTcN * 128;                // fp16 B tile
-    static constexpr int kRawRow = Q4 ? 32 : 64;         // quantised bytes of one row per step
+    static constexpr int kRawRow = NIB ? 32 : 64;        // quantised bytes of one row per step
     static constexpr int kBytes = kA + kB;                // 32 KB: stages stay 1024-aligned
 };
 
@@ -69,6 +69,10 @@ MOE_DEV uint64_t tc_desc_sw128(uint32_t saddr) {
 // 10-12 = 0), both K-major (bits 15, 16 = 0), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
 __host__ __device__ constexpr uint32_t tc_idesc_f16(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// The same with A and B bf16 (bits 7-9 and 10-12 = 1): the AWQ path with bf16 activations.
+__host__ __device__ constexpr uint32_t tc_idesc_bf16(int M, int N) {
+    return tc_idesc_f16(M, N) | (1u << 7) | (1u << 10);
 }
 
 MOE_DEV void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool accumulate) {
@@ -152,7 +156,9 @@ struct TcParams {
     const int32_t* mtile_start;  // tiles of kTcM rows per expert
     const int32_t* tokmap;
     int topk, E;
-    __half* ha;  // gate_up output: fp16(q_h * d_h) [P][I]
+    int group, ngk;  // AWQ: group size along K and K / group
+    int bf16ops;     // AWQ with bf16 activations: bf16 operands (exact x); otherwise fp16
+    __half* ha;  // gate_up output: the down GEMM's A rows [P][I] (fp16(q_h * d_h); AWQ: h in the operand type)
     float* out;         // down output: [P][H]
     int32_t* err;
 };
@@ -160,9 +166,10 @@ struct TcParams {
 constexpr int kTcProducers = 256;  // all threads copy A, dequantise B and run the epilogue
 constexpr int kTcThreads = kTcProducers;
 
-template <bool Q4, bool GATE_UP>
+template <int WF, bool GATE_UP>  // WF: 0 Q8_0, 1 Q4_0, 2 AWQ
 __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const TcParams p) {
-    using S = StageTc<Q4>;
+    constexpr bool NIB = WF != 0, AWQ = WF == 2;
+    using S = StageTc<NIB>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzled tiles need 1024-byte alignment
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -232,24 +239,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
     // raw B of this thread's (row tid/2, 32-block tid%2) per step, loaded into registers two
     // steps ahead of its dequantisation (no shared staging: 3 CTAs fit on an SM)
     struct RawB {
-        uint4 q0, q1;  // Q4: q0 only
-        uint16_t sc;
+        uint4 q0, q1;  // 4-bit formats: q0 only
+        uint16_t sc, z;  // block (Q4/Q8) or group (AWQ) scale; AWQ zero point
     };
     auto load_raw = [&](int ks, RawB& rb) {
         const int n = tid >> 1, h = tid & 1;
         int64_t qo, so;
         w_row(n, qo, so);
-        const uint4* src = reinterpret_cast<const uint4*>(wexp + qo + (int64_t)ks * S::kRawRow + h * (Q4 ? 16 : 32));
+        const uint4* src = reinterpret_cast<const uint4*>(wexp + qo + (int64_t)ks * S::kRawRow + h * (NIB ? 16 : 32));
         rb.q0 = __ldg(src);
-        if (!Q4) rb.q1 = __ldg(src + 1);
-        rb.sc = __ldg(reinterpret_cast<const unsigned short*>(wexp + so) + 2 * ks + h);
+        if (!NIB) rb.q1 = __ldg(src + 1);
+        if (AWQ) {  // the 32-block's group: bf16 scale, then the u8 zero points after all scales
+            const int grp = (ks * kTcK + h * 32) / p.group;
+            rb.sc = __ldg(reinterpret_cast<const unsigned short*>(wexp + so) + grp);
+            rb.z = __ldg(wexp + so + 2 * p.ngk + grp);
+        } else {
+            rb.sc = __ldg(reinterpret_cast<const unsigned short*>(wexp + so) + 2 * ks + h);
+        }
     };
     RawB rb0{}, rb1{};
     if (tid < kTcProducers) {
         if (0 < nsteps) load_raw(0, rb0);
         if (1 < nsteps) load_raw(1, rb1);
     }
-    const uint32_t idesc = tc_idesc_f16(kTcM, kTcN);
+    const bool bfo = AWQ && p.bf16ops;
+    const uint32_t idesc = bfo ? tc_idesc_bf16(kTcM, kTcN) : tc_idesc_f16(kTcM, kTcN);
+    auto pack2 = [&](float a, float b) -> uint32_t {
+        if (bfo) {
+            const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+            return *reinterpret_cast<const uint32_t*>(&v);
+        }
+        const __half2 v = __floats2half2_rn(a, b);
+        return *reinterpret_cast<const uint32_t*>(&v);
+    };
     const bool sbf = p.scale_bf16 != 0;
     bool ok = true;
     for (int s = 0; s < kStagesTc - 1; ++s) {
@@ -266,18 +288,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
             const RawB cur = rb0;
             rb0 = rb1;
             if (s + 2 < nsteps) load_raw(s + 2, rb1);
-            const float dw = scale_to_f32(cur.sc, sbf);
+            const float dw = AWQ ? __uint_as_float((uint32_t)cur.sc << 16) : scale_to_f32(cur.sc, sbf);
+            // 2^23 + n as float bits minus 2^23 + offset: exact n - 8 (Q4_0) or n - z (AWQ)
+            const float off = AWQ ? 8388608.0f + (float)cur.z : 8388616.0f;
             uint32_t pk[16];
-            if (Q4) {  // word i = elements 8i..8i+7, nibble j = element 8i+j, value nibble - 8
+            if (NIB) {  // word i = elements 8i..8i+7, nibble j = element 8i+j
                 const uint32_t qq[4] = {cur.q0.x, cur.q0.y, cur.q0.z, cur.q0.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
-                    for (int j = 0; j < 8; j += 2) {  // 2^23 + n as float bits, minus 2^23 + 8: exact n - 8
-                        const float v0 = (__uint_as_float(((qq[i] >> (4 * j)) & 15u) | 0x4B000000u) - 8388616.0f) * dw;
-                        const float v1 = (__uint_as_float(((qq[i] >> (4 * j + 4)) & 15u) | 0x4B000000u) - 8388616.0f) * dw;
-                        const __half2 b2 = __floats2half2_rn(v0, v1);
-                        pk[4 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
+                    for (int j = 0; j < 8; j += 2) {
+                        const float v0 = (__uint_as_float(((qq[i] >> (4 * j)) & 15u) | 0x4B000000u) - off) * dw;
+                        const float v1 = (__uint_as_float(((qq[i] >> (4 * j + 4)) & 15u) | 0x4B000000u) - off) * dw;
+                        pk[4 * i + j / 2] = pack2(v0, v1);
                     }
             } else {  // word i = elements 4i..4i+3 (int8)
                 const uint32_t qq[8] = {cur.q0.x, cur.q0.y, cur.q0.z, cur.q0.w, cur.q1.x, cur.q1.y, cur.q1.z, cur.q1.w};
@@ -288,8 +311,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
                         // byte b ^ 0x80 = q + 128: 2^23 + q + 128 as float bits, minus 2^23 + 128
                         const float v0 = (__uint_as_float((((qq[i] >> (8 * j)) & 0xffu) ^ 0x80u) | 0x4B000000u) - 8388736.0f) * dw;
                         const float v1 = (__uint_as_float((((qq[i] >> (8 * j + 8)) & 0xffu) ^ 0x80u) | 0x4B000000u) - 8388736.0f) * dw;
-                        const __half2 b2 = __floats2half2_rn(v0, v1);
-                        pk[2 * i + j / 2] = *reinterpret_cast<const uint32_t*>(&b2);
+                        pk[2 * i + j / 2] = pack2(v0, v1);
                     }
             }
             uint8_t* rowp = base + S::kA + n * 128;
@@ -355,14 +377,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
                     hv[u] = silu_mul(v[2 * u], v[2 * u + 1]);
                     amax = fmaxf(amax, fabsf(hv[u]));
                 }
-                if (amax > 65504.f) atomicExch(p.err, kErrRange);
-                const float dd = q8_scale(amax);
-                const float id = q8_inv(dd);
+                if (amax > 65504.f && !bfo) atomicExch(p.err, kErrRange);
                 uint32_t pk[16];
+                if (AWQ) {  // W4A16: h stays 16-bit (no requantisation)
 #pragma unroll
-                for (int u = 0; u < 32; u += 2) {
-                    const __half2 b2 = __floats2half2_rn((float)q8_quant(hv[u], id) * dd, (float)q8_quant(hv[u + 1], id) * dd);
-                    pk[u / 2] = *reinterpret_cast<const uint32_t*>(&b2);
+                    for (int u = 0; u < 32; u += 2) pk[u / 2] = pack2(hv[u], hv[u + 1]);
+                } else {
+                    const float dd = q8_scale(amax);
+                    const float id = q8_inv(dd);
+#pragma unroll
+                    for (int u = 0; u < 32; u += 2)
+                        pk[u / 2] = pack2((float)q8_quant(hv[u], id) * dd, (float)q8_quant(hv[u + 1], id) * dd);
                 }
                 uint4* dst = reinterpret_cast<uint4*>(p.ha + (int64_t)pos * I + u0);
 #pragma unroll

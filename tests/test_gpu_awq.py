@@ -81,3 +81,21 @@ def test_awq_export_decode_bit_exact():
             z_dev = d[:, 2 * ng:].astype(np.float32)
             W_dev = (nib.astype(np.float32) - np.repeat(z_dev, G, 1)) * np.repeat(s_dev, G, 1)
             assert np.array_equal(W_dev, W)
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("E,H,I,G,T,K", [(16, 512, 256, 128, 40, 8), (32, 1024, 384, 64, 100, 8)])
+def test_awq_tcgen05_gemm_path_matches_oracle(E, H, I, G, T, K, bf16):
+    # more than 24 tokens: the tcgen05 GEMMs on the 16-bit hidden rows (W4A16), bf16 / fp16 operands
+    eng, ws = awq_engine(E, H, I, G, seed=E + T + G)
+    xb, xf, ids, w = tokens(T, H, E, K, seed=T, bf16=bf16)
+    ids[0, 1] = -1
+    dt = torch.bfloat16 if bf16 else torch.float16
+    x = dev(xb.view(np.int16)).view(dt)
+    y = torch.empty((T, H), dtype=dt, device="cuda")
+    eng.forward(x, y, dev(ids), dev(w), capi.BF16 if bf16 else capi.F16, capi.BF16 if bf16 else capi.F16)
+    torch.cuda.synchronize()
+    assert eng.device_error() == 0
+    y_ref = O.moe_forward_awq(xf, ids, w, *ws, group=G)
+    rel, cos = parity(y.float().cpu().numpy(), y_ref)
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
