@@ -134,7 +134,8 @@ int moe_quantize_rows_q8_0(const void* x, int32_t dtype, int64_t rows, int64_t c
  * launch record 20 stamps per CTA (globaltimer ns unless noted; phase boundaries of the
  * fused kernel: start, routing, activation quantisation, first/last gate_up data, gate_up
  * done, grid barrier entered/passed, h requantised, first down data, down done, combine
- * done, SM clock at start/end, first down issue, barrier arrival fenced/observed, warp 0 down loop done / first down wait);
+ * done, SM clock at start/end, first down issue (split-K kernel: its chunk count and h
+ * slots), barrier arrival fenced/observed, warp 0 down loop done / first down wait);
  * enable == 0 turns it off.  When `out` is non-null, copies up to max_entries stamps of
  * the last launch (waits for the device).  *n_entries = CTAs x 20 while enabled. */
 int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64_t* out, int32_t max_entries,
