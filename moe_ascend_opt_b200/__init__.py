@@ -9,7 +9,7 @@ Importing the package loads the in-tree native libraries:
   (Int8-gemm/nanovllm_ops.cpp:349-431) for CUDA tensors.
 
 There is no CPU implementation: without the built libraries the import fails.
-Run ``python -m moe_ascend_opt_b200.build`` (or ``__graft_entry__.build()``).
+Run ``python moe_ascend_opt_b200/build.py`` (or ``__graft_entry__.build()``).
 """
 import os
 
@@ -21,7 +21,7 @@ TORCH_LIB_PATH = os.path.join(_HERE, "_nanovllm_b200.so")
 
 for _p in (LIB_PATH, TORCH_LIB_PATH):
     if not os.path.exists(_p):
-        raise ImportError(f"{_p} is missing: build the CUDA extension with `python -m moe_ascend_opt_b200.build`")
+        raise ImportError(f"{_p} is missing: build the CUDA extension with `python moe_ascend_opt_b200/build.py`")
 
 torch.ops.load_library(TORCH_LIB_PATH)
 

@@ -6,8 +6,9 @@
   ``torch.classes.nanovllm``), linked against libmoe_b200.so.
 
 Both land next to this file so that they travel with the source tree.
-Rebuilds only what is older than its sources.  ``python -m
-moe_ascend_opt_b200.build`` runs it.
+Rebuilds only what is older than its sources.  ``python
+moe_ascend_opt_b200/build.py`` runs it (a plain script: the package itself needs
+the libraries to import).
 """
 from __future__ import annotations
 

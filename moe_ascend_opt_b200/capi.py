@@ -49,7 +49,7 @@ def lib() -> C.CDLL:
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
-            raise ImportError(f"{LIB_PATH} is missing: build with `python -m moe_ascend_opt_b200.build`")
+            raise ImportError(f"{LIB_PATH} is missing: build with `python moe_ascend_opt_b200/build.py`")
         L = C.CDLL(LIB_PATH)
         L.moe_last_error.restype = C.c_char_p
         sig = {
