@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -38,9 +39,6 @@ Q4_BYTES_PER_EXPERT = (2 * I * H // 2) + (2 * I * (H // 32) * 2) + (H * I // 2) 
 Q8_BYTES_PER_EXPERT = (2 * I * H) + (2 * I * (H // 32) * 2) + (H * I) + (H * (I // 32) * 2)  # 5,013,504
 METRIC = "fused MoE layer µs & effective weight GB/s vs HBM peak, tokens 1–4096, 1/2/4/8 GPU"
 HBM_FALLBACK = 6650.0
-# DRAM bytes (read + write) per launch of moe_decode_kernel<Q4> at this workload, from the
-# ncu capture summarised in profiles/moe_decode_q4_T1.md.
-NCU_TRAFFIC_BYTES = 21330688
 
 
 def peaks():
@@ -478,8 +476,7 @@ def run_ours(args):
             ms = float(t.item())
         return ms
 
-    outdir = os.path.join(ROOT, "gpurun_out")
-    clk = ClockSampler(os.path.join(outdir if os.path.isdir(outdir) else "/tmp", f"clocks_rank{rank}.csv"), local)
+    clk = ClockSampler(os.path.join(args.clock_dir or tempfile.gettempdir(), f"clocks_rank{rank}.csv"), local)
     with clk:
         # soak so the clock record covers a loaded GPU, then the timed region
         t_soak = time.time()
@@ -520,7 +517,7 @@ def run_ours(args):
     if True:
         out["roofline"] = {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
                            "frac": round(value / peak, 4), "peak_source": peak_kind,
-                           "traffic": NCU_TRAFFIC_BYTES,
+                           "traffic": None,
                            "algorithmic_bytes_per_launch": round(avg_bytes),
                            "kernel": ("moe_decode_kernel" if T == 1 or args.quant == "awq" else
                                       "moe_decode_sk_kernel" if T <= 8 else
@@ -726,6 +723,7 @@ def main():
     ap.add_argument("--placement", default="contiguous", choices=["contiguous", "balanced"],
                     help="N>1: experts per rank in contiguous blocks or dealt by routing load")
     ap.add_argument("--cpu-worker", type=float, default=None)
+    ap.add_argument("--clock-dir", default=None, help="directory for the nvidia-smi clock samples (default: temp dir)")
     args = ap.parse_args()
     if args.cpu_worker is not None:
         return cpu_reference_worker(args.cpu_worker, args.tokens)

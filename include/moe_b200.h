@@ -147,8 +147,8 @@ int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64_t* out, in
  * cannot afford an allocation's implicit device synchronisation.  Same arguments and result
  * as moe_engine_forward, on an engine whose weights are loaded; its scratch comes from a
  * fixed 512 KiB array in device memory that every GPU loading this library holds until the
- * process exits.  Limit: 256 + 8*T*K*(I/32) + 4*T*K*I bytes must fit in 512 KiB (e.g. T*K <=
- * 160 at I = 768) and T must fit one decode launch; larger calls fail with MOE_ERR_INVALID.
+ * process exits.  Limit: 256 + 4*T*K*I bytes must fit in 512 KiB (e.g. T*K <=
+ * 170 at I = 768) and T must fit one decode launch; larger calls fail with MOE_ERR_INVALID.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress);
  * make that first call before any stream capture.  All calls share the one array: calls
  * that overlap on the GPU (other streams, other threads) race and must be serialised. */

@@ -18,6 +18,16 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 enum ErrCode : int32_t { kErrNone = 0, kErrGridBarrier = 1, kErrFullWait = 2, kErrEmptyWait = 3, kErrPeerWait = 4,
                          kErrRange = 5 };
 
+// Record a device error.  `err` is the engine's error word in mapped pinned host memory
+// (cudaHostAllocMapped), so the host reads it at the entry of the next call without a
+// device synchronisation: a plain system-scope store, made visible before the kernel
+// goes on.  The code is sticky until the host clears it.
+MOE_DEV void set_err(int32_t* err, int32_t code) {
+    if (!err) return;
+    *reinterpret_cast<volatile int32_t*>(err) = code;
+    __threadfence_system();
+}
+
 // Global expert id -> this engine's local id, or -1 for experts it does not hold: through
 // the placement map when one is set (local_of_global[gid]), else the contiguous block
 // [e_off, e_off + E).  Invalid ids are skipped like in the reference (moe_common.cpp:158).
@@ -187,7 +197,7 @@ MOE_DEV bool grid_barrier(unsigned long long* ctr, uint32_t nblocks, unsigned lo
         }
         if (it > 4096) __nanosleep(256);  // hot spin first: the barrier is on the critical path
     }
-    atomicExch(reinterpret_cast<int*>(err), kErrGridBarrier);
+    set_err(err, kErrGridBarrier);
     return false;
 }
 

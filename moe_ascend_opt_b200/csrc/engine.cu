@@ -72,6 +72,9 @@ struct moe_engine {
     float* h_ws = nullptr;
     int64_t h_cap = 0;  // positions
     uint32_t* bar = nullptr;
+    // error word: mapped pinned host memory, written by kernels (set_err) and read by the
+    // host at the entry of every call without synchronising; err is its device address
+    int32_t* herr = nullptr;
     int32_t* err = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     bool timed = false;
@@ -434,7 +437,11 @@ int ensure_workspace(moe_engine* eng, int64_t positions) {
     if (!eng->bar) {
         CUDA_TRY(cudaMalloc(&eng->bar, 256));
         CUDA_TRY(cudaMemset(eng->bar, 0, 256));
-        eng->err = reinterpret_cast<int32_t*>(eng->bar + 16);
+    }
+    if (!eng->herr) {
+        CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&eng->herr), 64, cudaHostAllocMapped));
+        *reinterpret_cast<volatile int32_t*>(eng->herr) = 0;
+        CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&eng->err), eng->herr, 0));
     }
     if (positions <= eng->h_cap) return MOE_OK;
     int64_t cap = eng->h_cap ? eng->h_cap : 64;
@@ -901,6 +908,37 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     return MOE_OK;
 }
 
+// Meaning of a device error code (ErrCode in common.cuh).
+const char* device_error_meaning(int32_t c) {
+    switch (c) {
+        case kErrGridBarrier: return "grid barrier wait expired";
+        case kErrFullWait: return "wait for weight data expired";
+        case kErrEmptyWait: return "wait for a free pipeline stage expired";
+        case kErrPeerWait: return "a peer rank did not arrive at the combine";
+        case kErrRange: return "an activation block exceeds the float16 range of the tcgen05 GEMM path";
+        default: return "unknown device error";
+    }
+}
+
+// Errors that kernels recorded are reported at the entry of the next call on the engine,
+// as the reference's TORCH_CHECKs would have raised: the host reads the mapped error word
+// (no synchronisation in the common case).  On an error the engine waits for the device,
+// clears the word and the barrier state so that later calls work, and fails this call.
+int check_sticky_error(moe_engine* eng, cudaStream_t st) {
+    if (!eng->herr) return MOE_OK;
+    const int32_t v = *reinterpret_cast<volatile int32_t*>(eng->herr);
+    if (v == 0) return MOE_OK;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone) {
+        CUDA_TRY(cudaDeviceSynchronize());
+        *reinterpret_cast<volatile int32_t*>(eng->herr) = 0;
+        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
+    }
+    return fail(MOE_ERR_DEVICE, std::string("an earlier launch on this engine failed on the device: error ") +
+                                    std::to_string(v) + " (" + device_error_meaning(v) +
+                                    "); its output is invalid; the engine state has been reset");
+}
+
 // =================================================================== C ABI
 extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (!cfg || !out) return fail(MOE_ERR_INVALID, "null argument");
@@ -969,6 +1007,7 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     cudaFree(eng->mbox);
     cudaFree(eng->h_ws);
     cudaFree(eng->bar);
+    if (eng->herr) cudaFreeHost(eng->herr);
     cudaFree(eng->timeline);
     cudaFree(eng->gws);
     if (eng->ev0) cudaEventDestroy(eng->ev0);
@@ -1141,6 +1180,7 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     if (T > 0 && (!x || !y || !topk_ids || !topk_w)) return fail(MOE_ERR_INVALID, "null tensor pointer");
     DeviceGuard g(eng->cfg.device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (int rc = check_sticky_error(eng, st)) return rc;
     if (T == 0) return MOE_OK;
     const int64_t H = eng->cfg.hidden_size;
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
@@ -1243,10 +1283,12 @@ extern "C" int moe_engine_device_error(moe_engine* eng, int32_t* code) {
     if (!code) return fail(MOE_ERR_INVALID, "null output");
     DeviceGuard g(eng->cfg.device);
     CUDA_TRY(cudaDeviceSynchronize());
-    int32_t v = 0;
-    CUDA_TRY(cudaMemcpy(&v, eng->err, 4, cudaMemcpyDeviceToHost));
+    const int32_t v = eng->herr ? *reinterpret_cast<volatile int32_t*>(eng->herr) : 0;
     *code = v;
-    if (v != 0) CUDA_TRY(cudaMemset(eng->bar, 0, 256));  // clear the error word and the barrier state
+    if (v != 0) {  // clear the error word and the barrier state
+        *reinterpret_cast<volatile int32_t*>(eng->herr) = 0;
+        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
+    }
     return MOE_OK;
 }
 
@@ -1340,7 +1382,6 @@ extern "C" int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64
     if (!enable && eng->timeline) {
         CUDA_TRY(cudaDeviceSynchronize());
         cudaFree(eng->timeline);
-    cudaFree(eng->gws);
         eng->timeline = nullptr;
         eng->timeline_ctas = 0;
     }
@@ -1360,11 +1401,11 @@ extern "C" int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64
 // synchronise the device) is not acceptable.  moe_engine_forward_noalloc runs the
 // fused decode kernel with the grid barrier between gate_up and down (the one
 // moe_engine_forward uses for AWQ) but takes its scratch (the h workspace, the
-// grid-barrier counter and the error word) from the fixed device array below instead of the engine's workspace, so it
+// grid-barrier counter) from the fixed device array below instead of the engine's workspace, so it
 // allocates nothing.  The array lives in every GPU that loads this library until
 // the process exits.
 constexpr size_t kNoAllocScratchBytes = 512 * 1024;
-constexpr size_t kNoAllocHeader = 256;  // barrier counter at 0, error word at 64
+constexpr size_t kNoAllocHeader = 256;  // grid-barrier counter at 0; h from byte 256
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
@@ -1400,7 +1441,7 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
     if (eng->p2p_active) return fail(MOE_ERR_STATE, "the no-allocation forward does not run the peer combine");
     const int64_t I = eng->cfg.intermediate_size;
     const int64_t P = T * K;
-    const size_t need = kNoAllocHeader + (size_t)8 * P * (I / 32) + (size_t)P * I * 4;
+    const size_t need = kNoAllocHeader + (size_t)P * I * 4;  // h is requantised in place
     if (need > kNoAllocScratchBytes)
         return fail(MOE_ERR_INVALID, "num_tokens x top_k x intermediate_size needs " + std::to_string(need) +
                                          " bytes of scratch; moe_engine_forward_noalloc holds at most " +
@@ -1413,8 +1454,9 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
     unsigned char* base = nullptr;
     if (int rc = noalloc_scratch(eng->cfg.device, &base)) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // every call reuses the array: clear the barrier counter and the error word (they
-    // must start at zero), leave h to be overwritten
+    if (int rc = check_sticky_error(eng, st)) return rc;
+    // every call reuses the array: clear the barrier counter (it must start at zero), leave
+    // h to be overwritten
     CUDA_TRY(cudaMemsetAsync(base, 0, kNoAllocHeader, st));
     DecodeParams& p = pl.p;
     p.act_bf16 = act_dtype == MOE_BF16;
@@ -1426,8 +1468,8 @@ extern "C" int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* 
     p.gu = eng->gu;
     p.dn = eng->dn;
     p.bar = reinterpret_cast<unsigned long long*>(base);
-    p.err = reinterpret_cast<int32_t*>(base + 64);
-    p.h_ws = reinterpret_cast<float*>(base + kNoAllocHeader + (size_t)8 * P * (I / 32));
+    p.err = eng->err;  // the engine's mapped error word: reported like moe_engine_forward's
+    p.h_ws = reinterpret_cast<float*>(base + kNoAllocHeader);
     p.dbg = nullptr;
     const int qt = eng->cfg.quant_type;
     return qt == MOE_Q4_0 ? launch_decode<kQ4>(pl, st)

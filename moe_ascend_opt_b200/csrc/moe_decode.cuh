@@ -126,7 +126,7 @@ MOE_DEV bool pc_finish(const DecodeParams& p, unsigned long long epoch, int cta,
                 if (it > 256) __nanosleep(256);
             }
         }
-        if (!ok) atomicExch(p.err, kErrPeerWait);
+        if (!ok) set_err(p.err, kErrPeerWait);
         s_pc_ok = ok;
     }
     __syncthreads();
@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
         int u, j0, n;
         while (c_use.next(u, j0, n)) {
             const int s = item % p.slots;
-            if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
+            if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { set_err(p.err, kErrFullWait); ok = false; break; }
             if (dbg && tid == 0) dbg[item == 0 ? 4 : 5] = global_ns();
             const bool valid = uslot < n;
             const uint8_t* rec = myring + (size_t)s * p.slot_bytes + (size_t)(valid ? uslot : 0) * 2 * (p.rs1 + p.ss1);
@@ -820,7 +820,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     for (int k2 = 0; ok && k2 < w2.n2; ++k2) {
         const int s = item % p.slots;
         if (dbg && tid == 0 && k2 == 0) dbg[19] = global_ns();
-        if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
+        if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { set_err(p.err, kErrFullWait); ok = false; break; }
         if (dbg && tid == 0 && k2 == 0) dbg[10] = global_ns();
         const uint8_t* st = myring + (size_t)s * p.slot_bytes;
         const int it = warp + k2 * kWarps;

@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_sk_kernel(const Decode
         int u, j0, n;
         while (c_use.next(u, j0, n)) {
             const int s = item % p.slots;
-            if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
+            if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { set_err(p.err, kErrFullWait); ok = false; break; }
             if (dbg && tid == 0 && item == 0) dbg[4] = global_ns();
             const bool valid = uslot < n;
             const uint8_t* rec = myring + (size_t)s * p.slot_bytes + (size_t)(valid ? uslot : 0) * 2 * (p.rs1 + p.ss1);
@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_sk_kernel(const Decode
     // ---------------- phase 2: split-K down for all H rows ----------------
     for (int k2 = 0; ok && k2 < n2; ++k2) {
         const int s = item % p.slots;
-        if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { atomicExch(p.err, kErrFullWait); ok = false; break; }
+        if (!mbar_wait(&mybar[s], (uint32_t)(item / p.slots) & 1u)) { set_err(p.err, kErrFullWait); ok = false; break; }
         if (dbg && tid == 0 && k2 == 0) dbg[10] = global_ns();
         const uint8_t* st = myring + (size_t)s * p.slot_bytes;
         const int u = (bb + k2) / nb2;

@@ -131,7 +131,7 @@ __global__ void quant_rows_f16_kernel(const uint8_t* x, int act_bf16, int rows, 
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
-        if (amax > 65504.f) atomicExch(err, kErrRange);
+        if (amax > 65504.f) set_err(err, kErrRange);
         const float dd = q8_scale(amax);
         const float id = q8_inv(dd);
         uint32_t packed[16];
@@ -341,10 +341,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
     }
     cp_async_wait<0>();
     if (tid == 0) tc_commit(&s_done);  // arrives once every MMA issued above has completed
-    if (!ok) atomicExch(p.err, kErrFullWait);
+    if (!ok) set_err(p.err, kErrFullWait);
     // bounded wait for the accumulator (on a failure path as well, before TMEM is released)
     if (!mbar_wait(&s_done, 0u)) {
-        atomicExch(p.err, kErrFullWait);
+        set_err(p.err, kErrFullWait);
         ok = false;
     }
     if (!ok) s_ok = 0;
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) grouped_gemm_tc_kernel(const Tc
                     hv[u] = silu_mul(v[2 * u], v[2 * u + 1]);
                     amax = fmaxf(amax, fabsf(hv[u]));
                 }
-                if (amax > 65504.f && !bfo) atomicExch(p.err, kErrRange);
+                if (amax > 65504.f && !bfo) set_err(p.err, kErrRange);
                 uint32_t pk[16];
                 if (AWQ) {  // W4A16: h stays 16-bit (no requantisation)
 #pragma unroll

@@ -339,7 +339,7 @@ std::tuple<at::Tensor, at::Tensor> quantize_rows(const at::Tensor& x) {
 
 }  // namespace
 
-TORCH_LIBRARY(nanovllm, m) {
+TORCH_LIBRARY_FRAGMENT(nanovllm, m) {
     m.class_<MoEInferHandle>("MoEInfer")
         .def(torch::init<int64_t, int64_t, int64_t, int64_t>())
         .def("quantize_and_store_expert", &MoEInferHandle::quantize_and_store_expert)

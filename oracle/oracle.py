@@ -23,7 +23,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libmoe_oracle.so")
 REF_BRIDGE_SO = os.path.join(HERE, "_ref", "ref_bridge.so")
 REF_EXT_SO = os.path.join(HERE, "_ref", "nanovllm_ext_ref.so")
-REF_SRC = os.environ.get("REF", "/root/reference/Int8-gemm")
+# The reference's Int8-gemm source directory: the REF environment variable, else a checkout
+# named `reference` beside this repository (absent on machines that only run the prebuilt files).
+REF_SRC = os.environ.get("REF") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference", "Int8-gemm")
 
 _P = C.c_void_p
 _lib = None

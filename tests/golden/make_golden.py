@@ -15,6 +15,13 @@ Fixtures:
   fwd_*.npz                MoEInfer forward, small shapes, Q8_0/Q4_0, f16/bf16 scales
   fwd_c1_q8.npz            BASELINE configs[0]: H2048 I768 E128 top8 T=1, Q8_0 from fp32 N(0,.02^2)
   fwd_c2_q4_T{1,4,8,32}    BASELINE configs[1]: same shape, Q4_0, token sweep
+  big_*.npz                large token counts at the sizes where the grouped GEMMs run by default
+                           (Qwen Q4_0/Q8_0 T=128/512/1024/4096, MiniMax Q4_0 T=1024), weights drawn
+                           directly in quantised form (tests/helpers.py random_q_weights); only the
+                           output rows of tests/helpers.py golden_rows are kept
+
+    python tests/golden/make_golden.py            # everything
+    python tests/golden/make_golden.py big        # only the large-T fixtures
 """
 import hashlib
 import json
@@ -29,7 +36,8 @@ sys.path.insert(0, ROOT)
 os.environ["NANOVLLM_TP_SIZE"] = "1"
 
 from oracle import oracle as O  # noqa: E402
-from tests.helpers import big_case_inputs, expert_weights_fp32, q_weights, tokens  # noqa: E402
+from tests.helpers import (big_case_inputs, expert_weights_fp32, golden_rows, q_weights,  # noqa: E402
+                           random_q_weights, tokens)
 
 
 def digest(*arrays) -> str:
@@ -116,9 +124,53 @@ def fwd_c2():
                             seed=np.int64(seed))
 
 
+BIG_CASES = [  # name, quant, H, I, E, T, seed
+    ("big_q4_T128", 1, 2048, 768, 128, 128, 501),
+    ("big_q4_T512", 1, 2048, 768, 128, 512, 502),
+    ("big_q4_T1024", 1, 2048, 768, 128, 1024, 503),
+    ("big_q4_T4096", 1, 2048, 768, 128, 4096, 504),
+    ("big_q8_T1024", 0, 2048, 768, 128, 1024, 505),
+    ("big_q8_T4096", 0, 2048, 768, 128, 4096, 506),
+    ("big_mm_q4_T1024", 1, 3072, 1536, 256, 1024, 507),
+]
+
+
+def fwd_big():
+    """Large-T cases through the reference engine; the kept rows and an input digest are stored."""
+    K = 8
+    for name, qt, H, I, E, T, seed in BIG_CASES:
+        gq, gd, dq, dd = random_q_weights(qt, E, H, I, seed)
+        xb, ids, w = big_case_inputs(T, seed, H=H, E=E)
+        eng = O.RefEngine(E, H, I, qt)
+        eng.store_repack(False, gq, gd, dq, dd)
+        y = eng.forward(xb, ids, w)
+        eng.close()
+        rows = golden_rows(T)
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), y_rows=y[rows], rows=rows,
+                            meta=np.array([qt, E, H, I, T, K, seed], np.int64),
+                            sha=np.array(digest(gq, gd, dq, dd, xb, ids, w)))
+        print("wrote", name, flush=True)
+
+
+def write_manifest():
+    files = sorted(f for f in os.listdir(HERE) if f.endswith(".npz"))
+    with open(os.path.join(HERE, "MANIFEST.json"), "w") as f:
+        json.dump({"generator": "tests/golden/make_golden.py",
+                   "reference": "Int8-gemm (MoEInfer, preprocess_moe_routing, quantize_block_q8_0, "
+                                "quantize_weight_only) built unmodified by oracle/Makefile with the scalar "
+                                "NEON and single-node NUMA shims, NANOVLLM_TP_SIZE=1",
+                   "files": files}, f, indent=1)
+    return files
+
+
 def main():
     if not O.have_reference():
         sys.exit("oracle/_ref/ref_bridge.so missing: run `make -C oracle ref` with the reference checkout")
+    if sys.argv[1:] == ["big"]:
+        fwd_big()
+        write_manifest()
+        sys.stdout.flush()
+        os._exit(0)
     route_cases()
     quant_cases()
     small = [
@@ -134,13 +186,8 @@ def main():
     fwd_case("q8_f16_T2_act16", 0, 16, 256, 128, 2, 8, 7, False, False)
     fwd_c1()
     fwd_c2()
-    files = sorted(f for f in os.listdir(HERE) if f.endswith(".npz"))
-    with open(os.path.join(HERE, "MANIFEST.json"), "w") as f:
-        json.dump({"generator": "tests/golden/make_golden.py",
-                   "reference": "Int8-gemm (MoEInfer, preprocess_moe_routing, quantize_block_q8_0, "
-                                "quantize_weight_only) built unmodified by oracle/Makefile with the scalar "
-                                "NEON and single-node NUMA shims, NANOVLLM_TP_SIZE=1",
-                   "files": files}, f, indent=1)
+    fwd_big()
+    files = write_manifest()
     print("wrote", len(files), "fixtures")
     sys.stdout.flush()
     os._exit(0)  # skip the reference thread pool's teardown

@@ -96,3 +96,33 @@ def digest_inputs(*arrays) -> str:
     for a in arrays:
         h.update(np.ascontiguousarray(a).tobytes())
     return h.hexdigest()
+
+
+def random_q_weights(qt: int, E: int, H: int, I: int, seed: int):
+    """Directly quantised random weights in the style of the reference's Q4_0 harness
+    (test/fused_moe_cpu_int4.py:74-115): uniform quant words (Q4_0: 8 nibbles per uint32;
+    Q8_0: int8 in [-127, 127]) and fp16 scales U(0,1) * s / sqrt(cols), s = 1/8 for Q4_0 and
+    2/127 for Q8_0.  Cheap to regenerate at full E, unlike fp32 weights quantised per expert."""
+    rng = np.random.default_rng(seed)
+
+    def q(rows, cols):
+        if qt == 1:
+            return rng.integers(0, 2 ** 32, size=(E, rows, cols // 8), dtype=np.uint64).astype(np.uint32).view(np.int32)
+        return rng.integers(-127, 128, size=(E, rows, cols), dtype=np.int8)
+
+    def d(rows, cols):
+        s = (1.0 / 8.0) if qt == 1 else (2.0 / 127.0)
+        return O.f32_to_f16_bits((rng.random((E, rows, cols // 32), dtype=np.float32) * s / np.sqrt(cols)).astype(np.float32))
+
+    gq = q(2 * I, H)
+    gd = d(2 * I, H)
+    dq = q(H, I)
+    dd = d(H, I)
+    return gq, gd, dq, dd
+
+
+def golden_rows(T: int, n: int = 32) -> np.ndarray:
+    """Token rows whose outputs a large-T golden fixture keeps: n rows spread over [0, T)."""
+    if T <= n:
+        return np.arange(T)
+    return np.unique(np.linspace(0, T - 1, n).round().astype(np.int64))

@@ -146,3 +146,19 @@ def test_reference_split_path_race():
         assert rel <= MAX_REL and cos >= MIN_COS
     for t in (1, 2):
         assert parity(y[t], y_ref[t])[1] < 0.9
+
+
+@pytest.mark.parametrize("name", ["big_q4_T128", "big_q8_T1024"])
+def test_large_t_fixture_rows_match_oracle(name):
+    """The large-T fixtures (the grouped-GEMM sizes): the oracle on the kept token rows
+    reproduces the reference's outputs of those rows."""
+    from tests.helpers import big_case_inputs, golden_rows, random_q_weights
+    f = load(name + ".npz")
+    qt, E, H, I, T, K, seed = (int(v) for v in f["meta"])
+    gq, gd, dq, dd = random_q_weights(qt, E, H, I, seed)
+    xb, ids, w = big_case_inputs(T, seed, H=H, E=E)
+    assert digest_inputs(gq, gd, dq, dd, xb, ids, w) == str(f["sha"])
+    rows = golden_rows(T)
+    y = O.moe_forward_q(qt, False, O.bf16_bits_to_f32(xb[rows]), ids[rows], w[rows], gq, gd, dq, dd)
+    rel, cos = parity(y, O.bf16_bits_to_f32(f["y_rows"]))
+    assert rel <= 5e-3 and cos >= 0.99999, (rel, cos)  # the fixture is bf16-rounded

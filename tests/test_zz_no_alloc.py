@@ -52,10 +52,36 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     eng = capi.Engine(E, H, I, 1)
     eng.load_quantized(torch.from_numpy(gq), torch.from_numpy(gd.view(np.int16)), torch.from_numpy(dq),
                        torch.from_numpy(dd.view(np.int16)), capi.F16)
-    T = 21  # 21 x 8 x 768 x 4 bytes of h alone exceed the 512 KiB array
+    T = 22  # 256 + 22 x 8 x 768 x 4 bytes of h exceed the 512 KiB array
     x = torch.zeros((T, H), dtype=torch.bfloat16, device="cuda")
     y = torch.zeros((T, H), dtype=torch.bfloat16, device="cuda")
     ids = torch.zeros((T, K), dtype=torch.int32, device="cuda")
     w = torch.zeros((T, K), dtype=torch.float32, device="cuda")
     with pytest.raises(capi.MoeError, match="scratch"):
         eng.forward_noalloc(x, y, ids, w, capi.BF16, capi.BF16)
+
+
+def test_noalloc_on_a_fresh_engine_allocates_nothing():
+    """First call on an engine that never ran moe_engine_forward: the device's free memory
+    does not move across the call, and the result then matches moe_engine_forward's."""
+    E, H, I, T, K = 32, 1024, 384, 2, 8
+    gq, gd, dq, dd = q_weights(1, E, H, I, 91)
+    eng = capi.Engine(E, H, I, 1)
+    eng.load_quantized(torch.from_numpy(gq), torch.from_numpy(gd.view(np.int16)), torch.from_numpy(dq),
+                       torch.from_numpy(dd.view(np.int16)), capi.F16)
+    xb, _, ids, w = tokens(T, H, E, K, 91)
+    x = dev(xb.view(np.int16)).view(torch.bfloat16)
+    idt, wt = dev(ids), dev(w)
+    y = torch.full((T, H), 3.0, dtype=torch.bfloat16, device="cuda")
+    y_ref = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    eng.forward_noalloc(x, y, idt, wt, capi.BF16, capi.BF16)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    eng.forward(x, y_ref, idt, wt, capi.BF16, capi.BF16)
+    torch.cuda.synchronize()
+    rel, cos = parity(y.float().cpu().numpy(), y_ref.float().cpu().numpy())
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
+    assert eng.device_error() == 0
