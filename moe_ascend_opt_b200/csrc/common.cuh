@@ -121,11 +121,13 @@ MOE_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait on a phase of an mbarrier; false when the budget ran out.
+// Bounded wait on a phase of an mbarrier; false when the budget ran out.  try_wait itself
+// suspends the thread for a while; a back-off sleep only starts after many polls, since a
+// sleeping warp wakes up late and the weight copies it waits for are on the critical path.
 MOE_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
     for (uint32_t it = 0; it < kSpinLimit; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (it > 64) __nanosleep(64);
+        if (it > 8192) __nanosleep(128);
     }
     return false;
 }

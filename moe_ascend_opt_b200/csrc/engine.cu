@@ -13,6 +13,7 @@
 
 #include "../../include/moe_b200.h"
 #include "common.cuh"
+#include "moe_decode_cl.cuh"
 #include "moe_decode_sk.cuh"
 #include "moe_gemm_tc.cuh"
 
@@ -56,6 +57,15 @@ struct moe_engine {
     // down weights re-laid for the split-K decode kernel (Q8_0 / Q4_0): [E][I/32][H/32] slices
     uint8_t* dk = nullptr;
     bool use_sk = true;  // decode through moe_decode_sk_kernel when the layout allows
+    // layouts of the cluster decode kernel: AWQ records gate_up [E][I/16][2][H/64] (agu) and
+    // down [E][H/32][I/64] (adn); Q8_0 / Q4_0 down row slices [E][H/32][I/32] (adn)
+    uint8_t* agu = nullptr;
+    uint8_t* adn = nullptr;
+    int cl_max_tokens = -1;  // cluster decode kernel (moe_decode_cl_kernel) up to this many tokens (-1: by format)
+    int cl_size = 4;         // its CTAs per cluster
+    int cl_clusters[3] = {-1, -1, -1};  // co-resident clusters per format (-1: not queried)
+    float* clpart = nullptr;  // its per-pair fp32 down rows [clpart_cap][H]
+    int64_t clpart_cap = 0;
     int32_t* emap = nullptr;  // optional placement map: global expert id -> local id or -1
     int32_t emap_n = 0;
     int32_t sk_cost_a = 3;  // its chunk cost model: streaming share per chunk vs one token of compute
@@ -516,7 +526,7 @@ bool plan_decode_sk(const moe_engine* eng, int T, int K, DecodePlan& pl) {
     off = round_up(off + 8 * kWarps * slots, 128);
     p.off_ring = (int)off;
     off += (int64_t)kWarps * slots * slot;
-    if (off > eng->max_smem - 256) return false;
+    if (off > eng->max_smem - 1024 - 256) return false;  // static shared memory (1 KB reserved + own)
     p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
     p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
     p.emap = eng->emap; p.emap_n = eng->emap_n;
@@ -567,7 +577,7 @@ bool plan_decode_lpr(const moe_engine* eng, int T, int K, int lpr0, DecodePlan& 
     off = round_up(off + 8 * kWarps * slots, 128);
     p.off_ring = (int)off;  // mbarriers sit in the 8*kWarps*slots bytes right before the ring
     off += (int64_t)kWarps * slots * slot;
-    if (off > eng->max_smem - 256) return false;
+    if (off > eng->max_smem - 1024 - 256) return false;  // static shared memory (1 KB reserved + own)
     p.rs1 = eng->rs1; p.ss1 = eng->ss1; p.rs2 = eng->rs2; p.ss2 = eng->ss2;
     p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
     p.emap = eng->emap; p.emap_n = eng->emap_n;
@@ -638,6 +648,271 @@ int launch_decode(const DecodePlan& pl, cudaStream_t st) {
 }
 
 }  // namespace
+
+// ------------------------------------------------------------------ cluster decode path
+// AWQ records of the cluster decode kernel, built from the row records: one thread per
+// (record, row r, lane column c) writes the 8 bytes lane c of an mma.sync m16n8k16 A
+// fragment reads for row r (16 nibbles: word w, nibble position i holds k = 16 (2w + (i%4)/2)
+// + 2c + 8 ((i%4)&1) + i/4 of the record's 64 k), and c == 0 the row's scale and zero point.
+// gate_up records [E][I/16][2][H/64] of 16 rows (560 B), down records [E][H/32][I/64] of 32
+// rows (1120 B).
+__global__ void awq_rec_pack_kernel(uint8_t* dst, const uint8_t* src, int64_t nrec, int gate_up, int64_t I, int64_t H,
+                                    int64_t G, int64_t rec_bytes, int64_t rs, int64_t ss) {
+    const int rows = gate_up ? 16 : 32;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= nrec * rows * 4) return;
+    const int64_t R = idx / (rows * 4);
+    const int r = (int)((idx >> 2) % rows), c = (int)(idx & 3);
+    const int64_t nk = (gate_up ? H : I) / kAwqK, ng = (gate_up ? H : I) / G;
+    const int64_t kh = R % nk;
+    int64_t t = R / nk;
+    const uint8_t* row;
+    const uint8_t* sc;
+    if (gate_up) {
+        const int64_t half = t & 1;
+        t >>= 1;
+        const int64_t ut = t % (I / 16), e = t / (I / 16);
+        const uint8_t* rec = src + (e * I + 16 * ut + r) * rec_bytes;
+        row = rec + half * rs;
+        sc = rec + 2 * rs + half * ss;
+    } else {
+        const int64_t rb = t % (H / 32), e = t / (H / 32);
+        row = src + (e * H + 32 * rb + r) * rec_bytes;
+        sc = row + rs;
+    }
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int jw = 0; jw < 2; ++jw)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int pp = i & 3, e2 = i >> 2;
+            const int64_t k = kh * kAwqK + 16 * (2 * jw + (pp >> 1)) + 2 * c + 8 * (pp & 1) + e2;
+            const uint32_t nib = (row[k >> 1] >> (4 * (k & 1))) & 0xFu;
+            w[jw] |= nib << (4 * i);
+        }
+    const int recb = gate_up ? kAwqGuRec : kAwqDnRec;
+    uint8_t* d = dst + R * recb;
+    *reinterpret_cast<uint2*>(d + r * 32 + c * 8) = make_uint2(w[0], w[1]);
+    if (c == 0) {
+        const int64_t grp = kh * kAwqK / G;
+        reinterpret_cast<uint16_t*>(d + rows * 32)[r] = reinterpret_cast<const uint16_t*>(sc)[grp];
+        d[rows * 34 + r] = sc[2 * ng + grp];
+    }
+}
+
+// Q8_0 / Q4_0 down row-slice records of the cluster decode kernel: [E][H/32][I/32] slices of
+// 32 rows x one 32-column block (32 x BB weight bytes, then 32 scales), from the row records.
+__global__ void pack_down_rowslices_kernel(uint8_t* dr, const uint8_t* dn, int64_t e0, int64_t e1, int64_t H,
+                                           int64_t I, int64_t rec, int rs2, int BB) {
+    const int64_t nb2 = I / 32, nsl = H / 32;
+    const int64_t n = (e1 - e0) * nsl * nb2 * 32;
+    const int64_t SB = 32 * BB + 64;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int l = (int)(i & 31);
+        const int64_t kc = (i >> 5) % nb2, sl = ((i >> 5) / nb2) % nsl, e = e0 + (i >> 5) / (nb2 * nsl);
+        const uint8_t* src = dn + (e * H + sl * 32 + l) * rec;
+        uint8_t* dst = dr + ((e * nsl + sl) * nb2 + kc) * SB;
+        const uint4* q = reinterpret_cast<const uint4*>(src + kc * BB);
+        uint4* d = reinterpret_cast<uint4*>(dst + (size_t)l * BB);
+        d[0] = q[0];
+        if (BB == 32) d[1] = q[1];
+        reinterpret_cast<uint16_t*>(dst + 32 * BB)[l] = reinterpret_cast<const uint16_t*>(src + rs2)[kc];
+    }
+}
+
+bool awq_recs_ok(const moe_engine* eng) {
+    const int64_t H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size, G = eng->cfg.group_size;
+    return eng->cfg.quant_type == MOE_AWQ && G % kAwqK == 0 && H % G == 0 && I % G == 0 && I % 16 == 0 &&
+           H % 32 == 0;
+}
+
+// The cluster kernel's weight layouts: AWQ records (from the row records) or the Q8_0 / Q4_0
+// down row slices.  Experts [e0, e1) of the row layouts changed.
+int build_cl_layout(moe_engine* eng, int64_t e0, int64_t e1, cudaStream_t st) {
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    if (eng->cfg.quant_type == MOE_AWQ) {
+        if (!awq_recs_ok(eng)) return MOE_OK;
+        const int64_t n1 = E * (I / 16) * 2 * (H / kAwqK), n2 = E * (H / 32) * (I / kAwqK);
+        if (!eng->agu) {
+            CUDA_TRY(cudaMalloc(&eng->agu, (size_t)n1 * kAwqGuRec));
+            CUDA_TRY(cudaMalloc(&eng->adn, (size_t)n2 * kAwqDnRec));
+        }
+        awq_rec_pack_kernel<<<(unsigned)((n1 * 64 + 255) / 256), 256, 0, st>>>(
+            eng->agu, eng->gu, n1, 1, I, H, eng->cfg.group_size, eng->unit_bytes(), eng->rs1, eng->ss1);
+        awq_rec_pack_kernel<<<(unsigned)((n2 * 128 + 255) / 256), 256, 0, st>>>(
+            eng->adn, eng->dn, n2, 0, I, H, eng->cfg.group_size, eng->row_bytes(), eng->rs2, 0);
+        CUDA_TRY(cudaGetLastError());
+        return MOE_OK;
+    }
+    if (H % 32 != 0) return MOE_OK;
+    const int BB = eng->cfg.quant_type == MOE_Q4_0 ? 16 : 32;
+    const size_t bytes = (size_t)E * (H / 32) * (I / 32) * (32 * BB + 64);
+    if (!eng->adn) CUDA_TRY(cudaMalloc(&eng->adn, bytes));
+    pack_down_rowslices_kernel<<<eng->num_sms * 8, 256, 0, st>>>(eng->adn, eng->dn, e0, e1, H, I, eng->row_bytes(),
+                                                                  eng->rs2, BB);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+struct ClPlan {
+    ClParams p;
+    size_t smem;
+};
+
+// Shared-memory plan of the cluster decode kernel for T tokens; false when it does not apply.
+bool plan_decode_cl(const moe_engine* eng, int T, int K, ClPlan& pl) {
+    const int qt = eng->cfg.quant_type;
+    const int E = (int)eng->cfg.num_experts, H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    const int cs = eng->cl_size;
+    if (T < 1 || T > 8 || T > eng->cl_max_tokens || !eng->adn) return false;
+    const bool awq = qt == MOE_AWQ;
+    if (awq && (!eng->agu || !awq_recs_ok(eng))) return false;
+    if (H % (32 * cs) != 0 || H % kClRowBlocks != 0 || 32 % cs != 0) return false;
+    // allowed K-splits Q: Q8/Q4 K-ranges of whole 32-blocks and 4-unit CTA slices; AWQ K-ranges
+    // of whole 64-k records and 16-unit CTA slices
+    int qmask = 0, qmin = 0, qmax = 0;
+    for (int lq = 0; (1 << lq) <= kClMaxQ; ++lq) {
+        const int q = 1 << lq;
+        if (I % q) break;
+        const int KR = I / q;
+        if (KR % cs) break;
+        const int UPC = KR / cs;
+        const bool okq = awq ? (KR % kAwqK == 0 && UPC % 16 == 0) : (KR % 32 == 0 && UPC % 4 == 0);
+        if (!okq) continue;
+        qmask |= 1 << lq;
+        if (!qmin) qmin = q;
+        qmax = q;
+    }
+    if (!qmask) return false;
+    const int TK = T * K, nb1 = H / 32, cap = T;
+    const int KRmax = I / qmin, UPCmax = KRmax / cs, RPC = H / cs;
+    ClParams& p = pl.p;
+    std::memset(&p, 0, sizeof(p));
+    p.qmask = qmask;
+    int64_t off = round_up((int64_t)(3 * TK + 5 * E + 4) * 4, 16);
+    p.off_wl = (int)off;
+    off = round_up(off + (int64_t)TK * qmax * 4, 128);
+    p.off_x = (int)off;
+    off += round_up(awq ? (int64_t)T * (H + 8) * 2 + (int64_t)T * (H / kAwqK) * 4
+                        : (int64_t)T * H + (int64_t)T * nb1 * 8, 128);
+    p.off_h = (int)off;
+    const int64_t hb = awq ? (int64_t)cap * (KRmax + 8) * 2 : (int64_t)cap * KRmax * 4;
+    p.hbuf_bytes = (int)hb;
+    off += round_up(hb, 128);
+    p.off_hq = (int)off;
+    if (awq) {
+        int64_t slots_bytes = 0;
+        for (int lq = 0; (1 << lq) <= kClMaxQ; ++lq) {
+            if (!((qmask >> lq) & 1)) continue;
+            const int rtn = 2 * (I >> lq) / cs / 16;  // gate_up row tiles of a CTA
+            const int nslot = (kClWarps + rtn - 1) / rtn + 1;
+            slots_bytes = std::max(slots_bytes, (int64_t)rtn * nslot * 16 * cap * 4);
+        }
+        off += round_up(std::max(slots_bytes, (int64_t)cap * (KRmax / kAwqK) * 4), 128);
+    } else {
+        off += round_up((int64_t)cap * KRmax + (int64_t)cap * (KRmax / 32) * 8, 128);
+    }
+    p.off_p = (int)off;
+    off += round_up((int64_t)cap * UPCmax * (awq ? 2 : 4), 128);
+    p.off_out = (int)off;
+    off += round_up((int64_t)cap * RPC * 4, 128);
+    // ring items of up to ~6 KB
+    int64_t maxitem;
+    if (awq) {
+        p.upi = 10;  // gate_up records per item (5.6 KB)
+        p.kpi = 5;   // down records per item (5.6 KB)
+        maxitem = std::max((int64_t)p.upi * kAwqGuRec, (int64_t)p.kpi * kAwqDnRec);
+    } else {
+        const int BB = qt == MOE_Q4_0 ? 16 : 32;
+        const int64_t ub = eng->unit_bytes(), SBq = 32 * BB + 64;
+        p.upi = (int)std::max<int64_t>(1, 6144 / ub);
+        p.kpi = (int)std::max<int64_t>(1, 6144 / SBq);
+        maxitem = std::max((int64_t)p.upi * ub, (int64_t)p.kpi * SBq);
+    }
+    off = round_up(off + 12 * kClWarps * kClInFlight, 128);  // mbarriers and item offsets
+    p.off_ring = (int)off;
+    int64_t ring = ((int64_t)eng->max_smem - 1024 - off) / kClWarps / 128 * 128;
+    if (const char* v = std::getenv("MOE_CL_RING_KB")) ring = std::min<int64_t>(ring, (int64_t)std::atoi(v) * 1024);
+    if (ring < maxitem) return false;
+    p.ring_bytes = (int)ring;
+    off += ring * kClWarps;
+    if (off > eng->max_smem - 1024) return false;
+    p.rs1 = eng->rs1; p.ss1 = eng->ss1;
+    p.E = E; p.e_off = eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
+    p.emap = eng->emap; p.emap_n = eng->emap_n;
+    p.scale_bf16 = eng->scale_bf16;
+    p.flags = eng->decode_flags;
+    pl.smem = (size_t)off;
+    return true;
+}
+
+template <int FMT, bool XBF>
+int setup_decode_cl(moe_engine* eng) {
+    auto kern = moe_decode_cl_kernel<FMT, XBF>;
+    static thread_local bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    // every plan fits in max_smem - 1024 bytes (the static shared memory)
+    const int dyn = eng->max_smem - 1024;
+    if (dev >= 64 || !attr_set[dev]) {
+        CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+        if (dev < 64) attr_set[dev] = true;
+    }
+    int& nc = eng->cl_clusters[FMT];
+    if (nc >= 0) return MOE_OK;
+    // the kernel holds all registers of an SM, so the count of co-resident clusters does not
+    // depend on the plan
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = eng->cl_size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(eng->cl_size * 16);
+    cfg.blockDim = dim3(kClThreads);
+    cfg.dynamicSmemBytes = (size_t)dyn;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    nc = std::min(n, eng->num_sms / eng->cl_size);
+    return MOE_OK;
+}
+
+template <int FMT, bool XBF>
+int launch_decode_cl(moe_engine* eng, ClPlan& pl, cudaStream_t st) {
+    if (int rc = setup_decode_cl<FMT, XBF>(eng)) return rc;
+    if (eng->cl_clusters[FMT] < 1) return fail(MOE_ERR_STATE, "no thread-block cluster fits");
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = eng->cl_size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(eng->cl_size * eng->cl_clusters[FMT]);
+    cfg.blockDim = dim3(kClThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_decode_cl_kernel<FMT, XBF>, pl.p));
+    return MOE_OK;
+}
+
+int ensure_clpart(moe_engine* eng, int64_t positions) {
+    if (positions <= eng->clpart_cap) return MOE_OK;
+    int64_t cap = eng->clpart_cap ? eng->clpart_cap : 64;
+    while (cap < positions) cap *= 2;
+    CUDA_TRY(cudaDeviceSynchronize());  // the old buffer may still be in use by queued work
+    if (eng->clpart) CUDA_TRY(cudaFree(eng->clpart));
+    eng->clpart = nullptr;
+    CUDA_TRY(cudaMalloc(&eng->clpart, (size_t)cap * eng->cfg.hidden_size * sizeof(float)));
+    eng->clpart_cap = cap;
+    return MOE_OK;
+}
 
 // ------------------------------------------------------------------ grouped-GEMM path
 // Large token counts: parallel routing, Q8_0 token rows, two grouped GEMMs on the
@@ -978,9 +1253,15 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
         else if (!wm && (bm == 16 || bm == 32 || bm == 64 || bm == 128)) eng->gemm_bm = bm;
     }
     if (const char* v = std::getenv("MOE_DECODE_SK")) eng->use_sk = std::atoi(v) != 0;
+    if (const char* v = std::getenv("MOE_CL_MAX_TOKENS")) eng->cl_max_tokens = std::atoi(v);
+    if (const char* v = std::getenv("MOE_CL_SIZE")) {
+        const int c = std::atoi(v);
+        if (c == 1 || c == 2 || c == 4 || c == 8) eng->cl_size = c;
+    }
     if (const char* v = std::getenv("MOE_SK_COST_A")) eng->sk_cost_a = std::max(0, std::atoi(v));
     if (const char* v = std::getenv("MOE_SK_MIN_CHUNKS")) eng->sk_min_chunks_per_cta = std::max(0, std::atoi(v));
     eng->max_smem = (int)prop.sharedMemPerBlockOptin;
+    if (eng->cl_max_tokens < 0) eng->cl_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 0;  // where it is faster
     int rc = MOE_OK;
     rc = alloc_q_layout(eng);
     if (rc == MOE_OK) rc = ensure_workspace(eng, 64);
@@ -1000,6 +1281,9 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     cudaFree(eng->gu);
     cudaFree(eng->dn);
     cudaFree(eng->dk);
+    cudaFree(eng->agu);
+    cudaFree(eng->adn);
+    cudaFree(eng->clpart);
     cudaFree(eng->emap);
     cudaFree(eng->part);
     for (int q = 0; q < kMaxPeers; ++q)
@@ -1047,6 +1331,7 @@ extern "C" int moe_engine_load_quantized(moe_engine* eng, const void* gu_qs, con
         if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
     }
     if (int rc = build_down_chunks(eng, 0, E, st)) return rc;
+    if (int rc = build_cl_layout(eng, 0, E, st)) return rc;
     CUDA_TRY(cudaStreamSynchronize(st));
     eng->scale_bf16 = scale_dtype == MOE_BF16;
     eng->loaded = true;
@@ -1088,8 +1373,10 @@ extern "C" int moe_engine_quantize_store_expert(moe_engine* eng, int64_t expert,
                                                                                        sb, stride);
     CUDA_TRY(cudaGetLastError());
     if (owned) CUDA_TRY(cudaFreeAsync(owned, st));
-    if (proj == 2)
+    if (proj == 2) {
         if (int rc = build_down_chunks(eng, expert, expert + 1, st)) return rc;
+        if (int rc = build_cl_layout(eng, expert, expert + 1, st)) return rc;
+    }
     CUDA_TRY(cudaStreamSynchronize(st));
     eng->scale_bf16 = 0;
     eng->loaded = true;
@@ -1132,6 +1419,7 @@ extern "C" int moe_engine_load_awq(moe_engine* eng, const void* w13_qw, const vo
             I, H, R2, eng->rs2, eng->ss2);
     }
     CUDA_TRY(cudaGetLastError());
+    if (int rc = build_cl_layout(eng, 0, E, st)) return rc;
     for (int i = 0; i < 6; ++i)
         if (owned[i]) CUDA_TRY(cudaFreeAsync(owned[i], st));
     CUDA_TRY(cudaStreamSynchronize(st));
@@ -1150,6 +1438,7 @@ extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t t
     }
     if (eng->dk)
         if (int rc = ensure_part(eng, std::min<int64_t>(max_tokens, 64))) return rc;
+    if (int rc = ensure_clpart(eng, std::min<int64_t>(max_tokens, 8) * top_k * kClMaxQ)) return rc;
     return ensure_workspace(eng, std::min<int64_t>(max_tokens, 64) * top_k);
 }
 
@@ -1214,6 +1503,50 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
             eng->timed = true;
         }
         return MOE_OK;
+    }
+    // decode sizes: the cluster kernel when it applies
+    if (!eng->p2p_active && T <= eng->cl_max_tokens) {
+        ClPlan cp;
+        const int qt = eng->cfg.quant_type;
+        const int fmt = qt == MOE_Q4_0 ? kQ4 : (qt == MOE_AWQ ? kAWQ : kQ8);
+        bool use = plan_decode_cl(eng, (int)T, (int)K, cp);
+        if (use) {
+            const bool xbf = act_dtype == MOE_BF16;
+            const int rc = fmt == kQ4 ? setup_decode_cl<kQ4, true>(eng)
+                                      : (fmt == kAWQ ? (xbf ? setup_decode_cl<kAWQ, true>(eng)
+                                                            : setup_decode_cl<kAWQ, false>(eng))
+                                                     : setup_decode_cl<kQ8, true>(eng));
+            if (rc) return rc;
+            use = eng->cl_clusters[fmt] >= 1;
+        }
+        if (use) {
+            if (int rc = ensure_clpart(eng, T * K * kClMaxQ)) return rc;
+            if (int rc = ensure_workspace(eng, 1)) return rc;  // combine counters and error word
+            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+            CUDA_TRY(cudaStreamIsCapturing(st, &cap));
+            const bool timed = cap == cudaStreamCaptureStatusNone;
+            if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
+            ClParams& p = cp.p;
+            p.act_bf16 = act_dtype == MOE_BF16;
+            p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+            p.x = x; p.y = y; p.ids = topk_ids; p.tw = topk_w;
+            p.gu = qt == MOE_AWQ ? eng->agu : eng->gu;
+            p.dn = eng->adn;
+            p.part = eng->clpart;
+            p.cnt = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(eng->bar) + 128);
+            p.err = eng->err;
+            p.dbg = eng->timeline;
+            const int rc = qt == MOE_Q4_0 ? launch_decode_cl<kQ4, true>(eng, cp, st)
+                           : qt == MOE_AWQ ? (p.act_bf16 ? launch_decode_cl<kAWQ, true>(eng, cp, st)
+                                                         : launch_decode_cl<kAWQ, false>(eng, cp, st))
+                                           : launch_decode_cl<kQ8, true>(eng, cp, st);
+            if (rc) return rc;
+            if (timed) {
+                CUDA_TRY(cudaEventRecord(eng->ev1, st));
+                eng->timed = true;
+            }
+            return MOE_OK;
+        }
     }
     // token slice that fits the decode kernel's shared-memory plan
     // (the split-K kernel when its plan fits)

@@ -356,6 +356,35 @@ MOE_DEV void quad_quant(const float (&v)[8], uint32_t qmask, float& d, int& sum,
 
 MOE_DEV uint32_t quad_mask(int lane) { return 0xfu << (lane & ~3); }
 
+// Token rows -> Q8_0 in shared memory, a quad of threads per 32-block (8 elements each, the
+// block maximum and sum by shuffles): the same result as quant_x_smem with a quarter of its
+// code.  nthreads must be a multiple of 4.
+template <bool Q4>
+MOE_DEV void quant_x_quad(const uint8_t* x, int act_bf16, int nrows, int cols, int8_t* q, float* d, int32_t* s,
+                          int tid, int nthreads) {
+    const int nblk = nrows * (cols >> 5), sub = tid & 3;
+    const uint32_t qm = quad_mask(tid & 31);
+    for (int g = tid >> 2; g < nblk; g += nthreads >> 2) {  // the 4 threads of a quad share g
+        float v[8];
+        const uint4 r = __ldg(reinterpret_cast<const uint4*>(x + (size_t)g * 64) + sub);
+        const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = scale_to_f32((uint16_t)(w4[i] & 0xffffu), act_bf16);
+            v[2 * i + 1] = scale_to_f32((uint16_t)(w4[i] >> 16), act_bf16);
+        }
+        float dd;
+        int sum;
+        uint2 o;
+        quad_quant<Q4>(v, qm, dd, sum, o);
+        *reinterpret_cast<uint2*>(q + (size_t)g * 32 + sub * 8) = o;
+        if (sub == 0) {
+            d[g] = dd;
+            if (Q4) s[g] = sum;
+        }
+    }
+}
+
 MOE_DEV void load8(const float* src, float (&v)[8]) {
     const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
     const float4 b = __ldcg(reinterpret_cast<const float4*>(src) + 1);
