@@ -117,6 +117,17 @@ int moe_engine_export_expert(moe_engine* eng, int64_t expert, int32_t which, voi
 int moe_route_topk(const float* logits, int64_t num_tokens, int64_t num_experts, int64_t top_k,
                    int32_t renormalize, int32_t* topk_ids, float* topk_w, void* stream);
 
+/* Router GEMM fused with the top-k of moe_route_topk: logits[t][e] = sum_h hidden[t][h] *
+ * router_w[e][h] (fp32 accumulate), then the selection and weights of moe_route_topk.  The
+ * reference computes the router logits outside its op and routes with
+ * Int8-gemm/test/fused_moe_cpu.py:20-37; this entry point is the attention-side pre-step
+ * that feeds moe_engine_forward directly.  hidden [T,H] (act_dtype MOE_F16 / MOE_BF16),
+ * router_w [E,H] (MOE_F16 / MOE_BF16 / MOE_F32), H a multiple of 8; logits [T,E] fp32 is
+ * written when non-null.  Device pointers, stream ordered. */
+int moe_route_gemm_topk(const void* hidden, int32_t act_dtype, const void* router_w, int32_t w_dtype,
+                        int64_t num_tokens, int64_t hidden_size, int64_t num_experts, int64_t top_k,
+                        int32_t renormalize, int32_t* topk_ids, float* topk_w, float* logits, void* stream);
+
 /* Stable counting sort of routed pairs by expert (Int8-gemm/moe_common.cpp:146-216):
  * counts [E], starts [E+1], token_map [T*K][2] = (t,k) per position, scatter_map [T*K]
  * (-1 for ids outside [0,E)).  Device pointers. */

@@ -23,7 +23,7 @@ SYMBOLS = [
     "moe_engine_device_error", "moe_engine_export_expert", "moe_route_topk", "moe_route_permute",
     "moe_quantize_rows_q8_0", "moe_engine_debug_timeline", "moe_engine_forward_noalloc", "moe_last_error",
     "moe_engine_p2p_mailbox", "moe_engine_p2p_connect", "moe_engine_p2p_enable", "moe_engine_p2p_covers",
-    "moe_engine_set_expert_map",
+    "moe_engine_set_expert_map", "moe_route_gemm_topk",
 ]
 
 
@@ -73,6 +73,7 @@ def lib() -> C.CDLL:
             "moe_engine_p2p_enable": [_P, _I32],
             "moe_engine_p2p_covers": [_P, _I64],
             "moe_engine_set_expert_map": [_P, _P, _I64],
+            "moe_route_gemm_topk": [_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _I32, _P, _P, _P, _P],
         }
         for name, args in sig.items():
             f = getattr(L, name)
@@ -95,6 +96,20 @@ def stream_handle(stream=None):
     import torch
     s = stream if stream is not None else torch.cuda.current_stream()
     return C.c_void_p(s.cuda_stream)
+
+
+def route_gemm_topk(hidden, router_w, top_k, renormalize=True, logits=None, stream=None):
+    """moe_route_gemm_topk on CUDA tensors: (ids int32 [T,K], weights fp32 [T,K])."""
+    import torch
+    T, H = hidden.shape
+    E = router_w.shape[0]
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=hidden.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=hidden.device)
+    code = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
+    call("moe_route_gemm_topk", hidden.data_ptr(), code[hidden.dtype], router_w.data_ptr(), code[router_w.dtype], T, H, E,
+         top_k, int(renormalize), ids.data_ptr(), w.data_ptr(), logits.data_ptr() if logits is not None else None,
+         stream_handle(stream))
+    return ids, w
 
 
 class Engine:

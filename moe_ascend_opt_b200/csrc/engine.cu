@@ -311,6 +311,91 @@ __global__ void route_topk_kernel(const float* logits, int T, int E, int K, int 
     }
 }
 
+// Router GEMM fused with top-k (the attention-side pre-step of a MoE layer): one CTA per
+// token.  The token row goes to shared memory as fp32; warp w computes the logits of
+// experts w, w + 8, ... (each lane a strided slice of H, 16-byte weight loads, a fixed
+// shuffle tree), then warp 0 selects the top K (K rounds of warp argmax, ties to the lower
+// id) and forms the weights as route_topk_kernel does.  Optional fp32 logits out.
+constexpr int kRgWarps = 8;
+__global__ void __launch_bounds__(kRgWarps * 32) route_gemm_topk_kernel(const void* x, int x_bf16, const void* wr,
+                                                                       int w_kind, int H, int E, int K, int renorm,
+                                                                       int32_t* ids, float* tw, float* logits_out) {
+    extern __shared__ float rg_smem[];
+    float* xs = rg_smem;          // [H]
+    float* lg = rg_smem + H;      // [E]
+    uint32_t* taken = reinterpret_cast<uint32_t*>(lg + E);  // [E/32]
+    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < H; i += blockDim.x) xs[i] = act_to_f32(x, (int64_t)t * H + i, x_bf16);
+    for (int i = tid; i < (E + 31) / 32; i += blockDim.x) taken[i] = 0;
+    __syncthreads();
+    for (int e = warp; e < E; e += kRgWarps) {
+        float acc = 0.f;
+        if (w_kind == MOE_F32) {
+            const float4* wrow = reinterpret_cast<const float4*>(static_cast<const float*>(wr) + (size_t)e * H);
+            for (int i = lane; i < H / 4; i += 32) {
+                const float4 v = __ldg(wrow + i);
+                acc = fmaf(v.x, xs[4 * i], acc);
+                acc = fmaf(v.y, xs[4 * i + 1], acc);
+                acc = fmaf(v.z, xs[4 * i + 2], acc);
+                acc = fmaf(v.w, xs[4 * i + 3], acc);
+            }
+        } else {
+            const uint4* wrow = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(wr) + (size_t)e * H);
+            const int wbf = w_kind == MOE_BF16;
+            for (int i = lane; i < H / 8; i += 32) {
+                const uint4 v = __ldg(wrow + i);
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc = fmaf(scale_to_f32((uint16_t)(w4[j] & 0xffffu), wbf), xs[8 * i + 2 * j], acc);
+                    acc = fmaf(scale_to_f32((uint16_t)(w4[j] >> 16), wbf), xs[8 * i + 2 * j + 1], acc);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            lg[e] = acc;
+            if (logits_out) logits_out[(size_t)t * E + e] = acc;
+        }
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    float sel_v[16];
+    int sel_i[16];
+    for (int k = 0; k < K; ++k) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < E; e += 32) {
+            if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
+            const float v = lg[e];
+            if (bi == 0x7fffffff || v > bv) { bv = v; bi = e; }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) taken[bi >> 5] |= 1u << (bi & 31);
+        __syncwarp();
+        sel_v[k] = bv;
+        sel_i[k] = bi;
+    }
+    if (lane == 0) {
+        const float m = sel_v[0];
+        float s = 0.f;
+        if (renorm) {
+            for (int k = 0; k < K; ++k) s += expf(sel_v[k] - m);
+        } else {
+            for (int e = 0; e < E; ++e) s += expf(lg[e] - m);
+        }
+        for (int k = 0; k < K; ++k) {
+            ids[(size_t)t * K + k] = sel_i[k];
+            tw[(size_t)t * K + k] = expf(sel_v[k] - m) / s;
+        }
+    }
+}
+
 int check_engine(moe_engine* eng) {
     if (!eng) return fail(MOE_ERR_INVALID, "engine is null");
     return MOE_OK;
@@ -1667,6 +1752,26 @@ extern "C" int moe_route_topk(const float* logits, int64_t T, int64_t E, int64_t
     const size_t smem = (size_t)wpb * ((E + 31) / 32) * 4;
     route_topk_kernel<<<(unsigned)((T + wpb - 1) / wpb), wpb * 32, smem, static_cast<cudaStream_t>(stream)>>>(
         logits, (int)T, (int)E, (int)K, renorm, ids, w);
+    CUDA_TRY(cudaGetLastError());
+    return MOE_OK;
+}
+
+extern "C" int moe_route_gemm_topk(const void* hidden, int32_t act_dtype, const void* router_w, int32_t w_dtype,
+                                   int64_t T, int64_t H, int64_t E, int64_t K, int32_t renorm, int32_t* ids,
+                                   float* topk_w, float* logits, void* stream) {
+    if (T < 0 || H <= 0 || E <= 0 || K <= 0 || K > 16 || K > E) return fail(MOE_ERR_INVALID, "need 1 <= top_k <= min(16, E)");
+    if (act_dtype != MOE_F16 && act_dtype != MOE_BF16) return fail(MOE_ERR_INVALID, "hidden must be f16 or bf16");
+    if (w_dtype != MOE_F16 && w_dtype != MOE_BF16 && w_dtype != MOE_F32)
+        return fail(MOE_ERR_INVALID, "router weight must be f16, bf16 or f32");
+    if (H % 8 != 0) return fail(MOE_ERR_INVALID, "hidden_size must be a multiple of 8");
+    const size_t smem = ((size_t)H + E + (E + 31) / 32) * 4;
+    if (smem > 200 * 1024) return fail(MOE_ERR_INVALID, "hidden_size + num_experts too large for the router kernel");
+    if (T == 0) return MOE_OK;
+    if (!hidden || !router_w || !ids || !topk_w) return fail(MOE_ERR_INVALID, "null pointer");
+    if (smem > 48 * 1024)
+        CUDA_TRY(cudaFuncSetAttribute(route_gemm_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    route_gemm_topk_kernel<<<(unsigned)T, kRgWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+        hidden, act_dtype == MOE_BF16, router_w, w_dtype, (int)H, (int)E, (int)K, renorm, ids, topk_w, logits);
     CUDA_TRY(cudaGetLastError());
     return MOE_OK;
 }

@@ -15,7 +15,7 @@
 //   torch.ops.nanovllm.moe_forward_npu_graph_out(..., ctx, out)            :406
 //   torch.classes.nanovllm.MoEGraphContext(moe, num_tokens, top_k, dtype)  :398-399
 //   torch.classes.nanovllm.NpuCallbackManager(stream_ptr, device_id)       :395-396 (no-op)
-//   new: moe_forward_partial, moe_route, moe_route_permute, quantize_rows_q8_0
+//   new: moe_forward_partial, moe_route, moe_route_gemm, moe_route_permute, quantize_rows_q8_0
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/custom_class.h>
@@ -310,6 +310,23 @@ std::tuple<at::Tensor, at::Tensor> moe_route(const at::Tensor& logits, int64_t K
     return {ids, w};
 }
 
+std::tuple<at::Tensor, at::Tensor> moe_route_gemm(const at::Tensor& hidden, const at::Tensor& weight, int64_t K,
+                                                  bool renormalize) {
+    TORCH_CHECK(hidden.is_cuda() && weight.is_cuda() && hidden.dim() == 2 && weight.dim() == 2 &&
+                    weight.size(1) == hidden.size(1),
+                "hidden [T,H] and router weight [E,H] must be CUDA tensors");
+    auto x = hidden.contiguous();
+    auto w = weight.contiguous();
+    c10::cuda::CUDAGuard g(x.get_device());
+    auto ids = at::empty({x.size(0), K}, x.options().dtype(at::kInt));
+    auto tw = at::empty({x.size(0), K}, x.options().dtype(at::kFloat));
+    check_rc(moe_route_gemm_topk(x.data_ptr(), dtype_code(x.scalar_type()), w.data_ptr(), dtype_code(w.scalar_type()),
+                                 x.size(0), x.size(1), w.size(0), K, renormalize ? 1 : 0, ids.data_ptr<int32_t>(),
+                                 tw.data_ptr<float>(), nullptr, cur_stream(x.get_device())),
+             "moe_route_gemm");
+    return {ids, tw};
+}
+
 std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> route_permute(const at::Tensor& ids, int64_t E) {
     TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kInt && ids.dim() == 2, "ids must be CUDA int32 [T,K]");
     auto x = ids.contiguous();
@@ -395,6 +412,7 @@ TORCH_LIBRARY_FRAGMENT(nanovllm, m) {
     m.def("moe_forward_npu_graph_out(Tensor hidden, Tensor topk_ids, Tensor topk_w, __torch__.torch.classes.nanovllm.MoEInfer moe, __torch__.torch.classes.nanovllm.MoEGraphContext ctx, Tensor(a!) out) -> ()");
     m.def("moe_forward_partial(Tensor hidden, Tensor topk_ids, Tensor topk_w, __torch__.torch.classes.nanovllm.MoEInfer moe) -> Tensor");
     m.def("moe_route(Tensor logits, int top_k, bool renormalize) -> (Tensor, Tensor)");
+    m.def("moe_route_gemm(Tensor hidden, Tensor router_weight, int top_k, bool renormalize) -> (Tensor, Tensor)");
     m.def("moe_route_permute(Tensor topk_ids, int num_experts) -> (Tensor, Tensor, Tensor, Tensor)");
     m.def("quantize_rows_q8_0(Tensor x) -> (Tensor, Tensor)");
 }
@@ -405,6 +423,7 @@ TORCH_LIBRARY_IMPL(nanovllm, CUDA, m) {
     m.impl("moe_forward_npu_graph_out", &moe_forward_graph_out);
     m.impl("moe_forward_partial", &moe_forward_partial);
     m.impl("moe_route", &moe_route);
+    m.impl("moe_route_gemm", &moe_route_gemm);
     m.impl("moe_route_permute", &route_permute);
     m.impl("quantize_rows_q8_0", &quantize_rows);
 }
