@@ -167,6 +167,16 @@ int moe_engine_forward_noalloc(moe_engine* eng, const void* x, void* y, const in
                                const float* topk_w, int64_t num_tokens, int64_t top_k,
                                int32_t act_dtype, int32_t out_dtype, void* stream);
 
+/* Packed-layout files (no counterpart in the reference, whose engine repacks every load:
+ * MoEInfer::store_quantized_weights_repack, Int8-gemm/moe_infer.cpp:96-282).
+ * moe_engine_save writes the engine's device-resident weight layouts (all formats, after any
+ * load call) with a header of the shape, format and record sizes and a checksum per section;
+ * moe_engine_load_file fills an engine created with the same moe_config from such a file by
+ * plain copies (no repacking) and fails with MOE_ERR_INVALID on a different shape or format,
+ * a truncated file or a checksum mismatch.  Both synchronise the device. */
+int moe_engine_save(moe_engine* eng, const char* path);
+int moe_engine_load_file(moe_engine* eng, const char* path);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* moe_last_error(void);
 

@@ -23,7 +23,7 @@ SYMBOLS = [
     "moe_engine_device_error", "moe_engine_export_expert", "moe_route_topk", "moe_route_permute",
     "moe_quantize_rows_q8_0", "moe_engine_debug_timeline", "moe_engine_forward_noalloc", "moe_last_error",
     "moe_engine_p2p_mailbox", "moe_engine_p2p_connect", "moe_engine_p2p_enable", "moe_engine_p2p_covers",
-    "moe_engine_set_expert_map", "moe_route_gemm_topk",
+    "moe_engine_set_expert_map", "moe_route_gemm_topk", "moe_engine_save", "moe_engine_load_file",
 ]
 
 
@@ -74,6 +74,8 @@ def lib() -> C.CDLL:
             "moe_engine_p2p_covers": [_P, _I64],
             "moe_engine_set_expert_map": [_P, _P, _I64],
             "moe_route_gemm_topk": [_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _I32, _P, _P, _P, _P],
+            "moe_engine_save": [_P, C.c_char_p],
+            "moe_engine_load_file": [_P, C.c_char_p],
         }
         for name, args in sig.items():
             f = getattr(L, name)
@@ -142,6 +144,12 @@ class Engine:
     def forward_noalloc(self, x, y, ids, w, act_dtype, out_dtype, stream=None):
         call("moe_engine_forward_noalloc", self.h, x.data_ptr(), y.data_ptr(), ids.data_ptr(), w.data_ptr(),
              x.shape[0], ids.shape[1], act_dtype, out_dtype, stream_handle(stream))
+
+    def save(self, path):
+        call("moe_engine_save", self.h, os.fsencode(path))
+
+    def load_file(self, path):
+        call("moe_engine_load_file", self.h, os.fsencode(path))
 
     def reserve(self, T, K):
         call("moe_engine_reserve", self.h, T, K)

@@ -1968,6 +1968,137 @@ extern "C" int moe_engine_p2p_enable(moe_engine* eng, int32_t on) {
     return MOE_OK;
 }
 
+// =================================================================== packed-layout files
+// A file of an engine's device-resident layouts, so that a later process loads them with
+// plain copies instead of repacking from the quantised tensors.  Little-endian:
+//   "MOEB200\0" | u32 version | u32 section count | config (E, H, I as i64; quant type,
+//   group size, scale dtype, rs1, ss1, rs2, ss2 as i32) | per section: u32 id, u32 0,
+//   u64 bytes, u64 file offset, u64 FNV-1a checksum | data (4 KiB-aligned sections).
+namespace {
+constexpr char kFileMagic[8] = {'M', 'O', 'E', 'B', '2', '0', '0', '\0'};
+constexpr uint32_t kFileVersion = 1;
+struct FileConfig {
+    int64_t E, H, I;
+    int32_t quant_type, group_size, scale_bf16, rs1, ss1, rs2, ss2, pad;
+};
+struct FileSection {
+    uint32_t id, zero;
+    uint64_t bytes, offset, checksum;
+};
+
+uint64_t fnv1a(const uint8_t* p, size_t n, uint64_t h = 1469598103934665603ull) {
+    for (size_t i = 0; i < n; ++i) h = (h ^ p[i]) * 1099511628211ull;
+    return h;
+}
+
+// The engine's device buffers that a file holds: (id, pointer, bytes).
+struct Buf {
+    uint32_t id;
+    uint8_t** ptr;
+    size_t bytes;
+};
+std::vector<Buf> engine_buffers(moe_engine* eng) {
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    std::vector<Buf> v;
+    v.push_back({1, &eng->gu, (size_t)E * I * eng->unit_bytes()});
+    v.push_back({2, &eng->dn, (size_t)E * H * eng->row_bytes()});
+    if (eng->dk) v.push_back({3, &eng->dk, (size_t)E * (I / 32) * (H / 32) * sk_slice_bytes(eng)});
+    if (eng->cfg.quant_type == MOE_AWQ) {
+        if (eng->agu) v.push_back({4, &eng->agu, (size_t)E * (I / 16) * 2 * (H / kAwqK) * kAwqGuRec});
+        if (eng->adn) v.push_back({5, &eng->adn, (size_t)E * (H / 32) * (I / kAwqK) * kAwqDnRec});
+    } else if (eng->adn) {
+        const int BB = eng->cfg.quant_type == MOE_Q4_0 ? 16 : 32;
+        v.push_back({5, &eng->adn, (size_t)E * (H / 32) * (I / 32) * (32 * BB + 64)});
+    }
+    return v;
+}
+}  // namespace
+
+extern "C" int moe_engine_save(moe_engine* eng, const char* path) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!path) return fail(MOE_ERR_INVALID, "null path");
+    if (!eng->loaded) return fail(MOE_ERR_STATE, "no weights loaded");
+    DeviceGuard g(eng->cfg.device);
+    CUDA_TRY(cudaDeviceSynchronize());
+    std::vector<Buf> bufs = engine_buffers(eng);
+    FileConfig fc{eng->cfg.num_experts, eng->cfg.hidden_size, eng->cfg.intermediate_size, eng->cfg.quant_type,
+                  eng->cfg.group_size, eng->scale_bf16, eng->rs1, eng->ss1, eng->rs2, eng->ss2, 0};
+    std::vector<FileSection> secs(bufs.size());
+    uint64_t off = round_up(sizeof(kFileMagic) + 8 + sizeof(FileConfig) + bufs.size() * sizeof(FileSection), 4096);
+    std::vector<std::vector<uint8_t>> host(bufs.size());
+    for (size_t i = 0; i < bufs.size(); ++i) {
+        host[i].resize(bufs[i].bytes);
+        CUDA_TRY(cudaMemcpy(host[i].data(), *bufs[i].ptr, bufs[i].bytes, cudaMemcpyDeviceToHost));
+        secs[i] = {bufs[i].id, 0, bufs[i].bytes, off, fnv1a(host[i].data(), bufs[i].bytes)};
+        off = round_up(off + bufs[i].bytes, 4096);
+    }
+    FILE* f = std::fopen(path, "wb");
+    if (!f) return fail(MOE_ERR_INVALID, std::string("cannot open ") + path + " for writing");
+    const uint32_t hdr[2] = {kFileVersion, (uint32_t)bufs.size()};
+    bool ok = std::fwrite(kFileMagic, 1, 8, f) == 8 && std::fwrite(hdr, 4, 2, f) == 2 &&
+              std::fwrite(&fc, sizeof(fc), 1, f) == 1 &&
+              std::fwrite(secs.data(), sizeof(FileSection), secs.size(), f) == secs.size();
+    for (size_t i = 0; ok && i < bufs.size(); ++i)
+        ok = std::fseek(f, (long)secs[i].offset, SEEK_SET) == 0 &&
+             std::fwrite(host[i].data(), 1, host[i].size(), f) == host[i].size();
+    ok = (std::fclose(f) == 0) && ok;
+    if (!ok) return fail(MOE_ERR_INVALID, std::string("write to ") + path + " failed");
+    return MOE_OK;
+}
+
+extern "C" int moe_engine_load_file(moe_engine* eng, const char* path) {
+    if (int rc = check_engine(eng)) return rc;
+    if (!path) return fail(MOE_ERR_INVALID, "null path");
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(MOE_ERR_INVALID, std::string("cannot open ") + path);
+    struct Closer {
+        FILE* f;
+        ~Closer() { std::fclose(f); }
+    } closer{f};
+    char magic[8];
+    uint32_t hdr[2];
+    FileConfig fc;
+    if (std::fread(magic, 1, 8, f) != 8 || std::memcmp(magic, kFileMagic, 8) != 0)
+        return fail(MOE_ERR_INVALID, "not a packed-layout file (bad magic)");
+    if (std::fread(hdr, 4, 2, f) != 2 || hdr[0] != kFileVersion || hdr[1] == 0 || hdr[1] > 16)
+        return fail(MOE_ERR_INVALID, "unsupported packed-layout file version or section count");
+    if (std::fread(&fc, sizeof(fc), 1, f) != 1) return fail(MOE_ERR_INVALID, "truncated header");
+    if (fc.E != eng->cfg.num_experts || fc.H != eng->cfg.hidden_size || fc.I != eng->cfg.intermediate_size ||
+        fc.quant_type != eng->cfg.quant_type || (fc.quant_type == MOE_AWQ && fc.group_size != eng->cfg.group_size))
+        return fail(MOE_ERR_INVALID, "the file's shape or quantisation differs from the engine's");
+    std::vector<FileSection> secs(hdr[1]);
+    if (std::fread(secs.data(), sizeof(FileSection), secs.size(), f) != secs.size())
+        return fail(MOE_ERR_INVALID, "truncated section table");
+    DeviceGuard g(eng->cfg.device);
+    if (int rc = alloc_q_layout(eng)) return rc;  // the row layouts (and the split-K chunks)
+    if (fc.rs1 != eng->rs1 || fc.ss1 != eng->ss1 || fc.rs2 != eng->rs2 || fc.ss2 != eng->ss2)
+        return fail(MOE_ERR_INVALID, "the file's record layout differs from this build's");
+    const int64_t E = eng->cfg.num_experts, H = eng->cfg.hidden_size, I = eng->cfg.intermediate_size;
+    // the cluster kernel's layouts are allocated on demand, as build_cl_layout does
+    for (const FileSection& sc : secs) {
+        if (sc.id == 4 && !eng->agu) CUDA_TRY(cudaMalloc(&eng->agu, sc.bytes));
+        if (sc.id == 5 && !eng->adn) CUDA_TRY(cudaMalloc(&eng->adn, sc.bytes));
+    }
+    (void)E; (void)H; (void)I;
+    std::vector<Buf> bufs = engine_buffers(eng);
+    std::vector<uint8_t> host;
+    for (const FileSection& sc : secs) {
+        const Buf* b = nullptr;
+        for (const Buf& x : bufs)
+            if (x.id == sc.id) b = &x;
+        if (!b || b->bytes != sc.bytes) return fail(MOE_ERR_INVALID, "section " + std::to_string(sc.id) + " does not fit the engine");
+        host.resize(sc.bytes);
+        if (std::fseek(f, (long)sc.offset, SEEK_SET) != 0 || std::fread(host.data(), 1, sc.bytes, f) != sc.bytes)
+            return fail(MOE_ERR_INVALID, "truncated section " + std::to_string(sc.id));
+        if (fnv1a(host.data(), sc.bytes) != sc.checksum)
+            return fail(MOE_ERR_INVALID, "checksum mismatch in section " + std::to_string(sc.id));
+        CUDA_TRY(cudaMemcpy(*b->ptr, host.data(), sc.bytes, cudaMemcpyHostToDevice));
+    }
+    eng->scale_bf16 = fc.scale_bf16;
+    eng->loaded = true;
+    return MOE_OK;
+}
+
 // =================================================================== expert placement
 extern "C" int moe_engine_set_expert_map(moe_engine* eng, const int32_t* local_of_global, int64_t num_global) {
     if (int rc = check_engine(eng)) return rc;

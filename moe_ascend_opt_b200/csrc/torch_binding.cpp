@@ -370,6 +370,16 @@ TORCH_LIBRARY_FRAGMENT(nanovllm, m) {
                  return (int64_t)reinterpret_cast<intptr_t>(s->eng);
              })
         .def("set_group_size", &MoEInferHandle::set_group_size)
+        .def("save",  // the device-resident packed layouts to a file (include/moe_b200.h, moe_engine_save)
+             [](const c10::intrusive_ptr<MoEInferHandle>& s, const std::string& path) {
+                 TORCH_CHECK(s->eng, "no weights loaded");
+                 check_rc(moe_engine_save(s->eng, path.c_str()), "save");
+             })
+        .def("load_file",  // fill the engine from such a file, no repacking
+             [](const c10::intrusive_ptr<MoEInferHandle>& s, const std::string& path) {
+                 s->ensure_engine();
+                 check_rc(moe_engine_load_file(s->eng, path.c_str()), "load_file");
+             })
         .def("p2p_mailbox", &MoEInferHandle::p2p_mailbox)
         .def("p2p_connect", &MoEInferHandle::p2p_connect)
         .def("p2p_covers", &MoEInferHandle::p2p_covers)
