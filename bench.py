@@ -41,6 +41,15 @@ METRIC = "fused MoE layer µs & effective weight GB/s vs HBM peak, tokens 1–40
 HBM_FALLBACK = 6650.0
 
 
+def tflops_peaks():
+    """Sustained dense bf16 TFLOP/s of this pool's B200s (MEASURED_PEAKS.json), else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"])
+    except Exception:
+        return 1400.0
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -677,8 +686,13 @@ def run_ours(args):
         # AWQ W4A16 g128, Qwen shape, batch 1, softmax and Zipf(1.2) routing
         out["north_star"] = {r: extra_block("awq", "qwen", r, 1, min(args.steps, 4000), dev, peak)
                              for r in ("softmax", "zipf")}
+    if world == 1 and args.stack:
+        out["stack"] = stack_block(args.stack, "awq", "zipf", dev, peak, tflops_peaks())
     if world == 1 and not args.no_cpu and default_wl:
         out["cpu_baseline"] = cpu_baseline(T)
+        if "stack" in out and (out["cpu_baseline"] or {}).get("ms_per_step"):
+            # reference CPU engine per layer (Q4_0 T=1, the nearest format it has) x layers: a proxy
+            out["stack"]["cpu_proxy_decode_T1_ms_per_step"] = round(out["cpu_baseline"]["ms_per_step"] * args.stack, 3)
     if args.sweep and world == 1:
         out["sweep"] = sweep(handles, dev, args, H, I, E, bpe)
     if rank == 0:
@@ -753,6 +767,74 @@ def extra_block(quant, shape, routing, T, steps, dev, peak, nsets=16):
     return out
 
 
+def stack_block(nlayers, quant, routing, dev, peak, tflops_peak, decode_tokens=(1, 4, 8), prefill_tokens=4096,
+                steps=20):
+    """a stack of `nlayers` independent Qwen-shaped layers, one step = one
+    forward through every layer (CUDA graph of the whole stack).  Decode steps at batch
+    `decode_tokens`, one prefill-sized step; routing as given."""
+    import torch
+    H_, I_, E_ = SHAPES["qwen"]
+    bpe = bytes_per_expert(quant, H_, I_)
+    handles = [make_layer(quant, "qwen", 5000 + l, dev, 0, E_, 1, 0) for l in range(nlayers)]
+    torch.cuda.synchronize()
+    g = torch.Generator(device=dev)
+    g.manual_seed(23)
+    res = {"layers": nlayers, "quant": quant, "routing": routing}
+    for T in list(decode_tokens) + [prefill_tokens]:
+        for h in handles:
+            h.reserve(T, K)
+        xs, idss, wss, nb = [], [], [], []
+        for l in range(nlayers):
+            xs.append(torch.randn((T, H_), generator=g, device=dev).to(torch.bfloat16))
+            ids, w = make_routing(routing, T, E_, K, g, dev)
+            idss.append(ids); wss.append(w); nb.append(int(torch.unique(ids).numel()) * bpe)
+        outs = [torch.empty((T, H_), dtype=torch.bfloat16, device=dev) for _ in range(nlayers)]
+        ctxs = [torch.classes.nanovllm.MoEGraphContext(h, T, K, 1) for h in handles]
+
+        def stack():
+            for l in range(nlayers):
+                torch.ops.nanovllm.moe_forward_npu_graph_out(xs[l], idss[l], wss[l], handles[l], ctxs[l], outs[l])
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            stack()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            stack()
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        reps = steps if T <= 64 else max(3, steps // 4)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        byts = sum(nb)
+        flops = 6.0 * T * K * H_ * I_ * nlayers
+        key = f"decode_T{T}" if T in decode_tokens else f"prefill_T{T}"
+        res[key] = {"ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / nlayers, 3),
+                    "weight_GBps": round(byts / (ms * 1e-3) / 1e9, 1),
+                    "hbm_frac": round(byts / (ms * 1e-3) / 1e9 / peak, 4),
+                    "TFLOPs": round(flops / (ms * 1e-3) / 1e12, 2),
+                    "tensor_frac": round(flops / (ms * 1e-3) / 1e12 / tflops_peak, 4),
+                    "active_weight_bytes": byts}
+        errs = sorted({int(h.device_error()) for h in handles} - {0})
+        if errs:
+            res[key]["device_errors"] = errs
+        del xs, idss, wss, outs, ctxs, gr
+        torch.cuda.empty_cache()
+    del handles
+    torch.cuda.empty_cache()
+    return res
+
+
 def sweep(handles, dev, args, H, I, E, bpe):
     """Eager per-T timing (events) for the token sweep of BASELINE configs[1]."""
     import torch
@@ -798,6 +880,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-north-star", action="store_true", help="skip the AWQ W4A16 T=1 blocks")
+    ap.add_argument("--stack", type=int, default=0,
+                    help="add a block for an N-layer AWQ stack (BASELINE configs[4]: decode 1/4/8, prefill 4096)")
     ap.add_argument("--sweep", action="store_true")
     ap.add_argument("--quant", default="q4", choices=["q4", "q8", "awq"])
     ap.add_argument("--shape", default="qwen", choices=["qwen", "minimax"])

@@ -90,6 +90,16 @@ int moe_engine_forward(moe_engine* eng, const void* x, void* y, const int32_t* t
                        const float* topk_w, int64_t num_tokens, int64_t top_k, int32_t act_dtype,
                        int32_t out_dtype, void* stream);
 
+/* Dense MLP (a shared expert, or a dense FFN layer) through the same fused kernels:
+ * y = down(SiLU(gate x) * up x) of local expert `expert` for every token, i.e.
+ * moe_engine_forward with top_k = 1, that expert and weight 1 (the routing is kept in an
+ * engine buffer, allocated on the first call with more tokens than before).  A shared expert
+ * fuses into the routed layer without this call: load it as one more expert and pass its id
+ * as an extra top-k column with its gate weight (1, or the model's shared-expert gate).
+ * No counterpart in the reference, whose engine only serves routed experts. */
+int moe_engine_forward_dense(moe_engine* eng, int64_t expert, const void* x, void* y, int64_t num_tokens,
+                             int32_t act_dtype, int32_t out_dtype, void* stream);
+
 /* Reserve the forward's device workspace for up to max_tokens x top_k so that
  * later forwards allocate nothing (needed before CUDA graph capture).
  * Replaces the role of NumaBufferPool::ensure_capacity (Int8-gemm/moe_common.cpp:57-111). */
@@ -204,8 +214,14 @@ int moe_engine_p2p_covers(moe_engine* eng, int64_t num_tokens);
  * [expert_offset, expert_offset + num_experts) by an explicit map: local_of_global[g] is
  * the local index (0 .. num_experts-1) of global expert g on this engine, or -1 when another
  * engine holds it; every local index appears once.  The weights loaded into local slot l
- * must be those of the global expert mapped to l.  Copied to the device (synchronises). */
+ * must be those of the global expert mapped to l.  An entry `l | MOE_REPLICATED` marks a hot
+ * expert that every rank holds (replication of hot experts): this engine then computes its
+ * routed pairs only for tokens t with (t + g) % world == rank, from moe_engine_set_replica_split,
+ * so that each pair is computed once across the ranks.  Copied to the device (synchronises). */
+#define MOE_REPLICATED (1 << 30)
 int moe_engine_set_expert_map(moe_engine* eng, const int32_t* local_of_global, int64_t num_global);
+/* This engine's rank and the world size for the replicated experts of its map (default 0 of 1). */
+int moe_engine_set_replica_split(moe_engine* eng, int32_t rank, int32_t world);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libmoe_b200.so")
 
 MOE_OK, MOE_ERR_INVALID, MOE_ERR_CUDA, MOE_ERR_STATE, MOE_ERR_DEVICE = 0, -1, -2, -3, -4
 Q8_0, Q4_0, AWQ = 0, 1, 2
+REPLICATED = 1 << 30
 F16, BF16, F32 = 0, 1, 2
 
 # every symbol include/moe_b200.h declares
@@ -24,6 +25,7 @@ SYMBOLS = [
     "moe_quantize_rows_q8_0", "moe_engine_debug_timeline", "moe_engine_forward_noalloc", "moe_last_error",
     "moe_engine_p2p_mailbox", "moe_engine_p2p_connect", "moe_engine_p2p_enable", "moe_engine_p2p_covers",
     "moe_engine_set_expert_map", "moe_route_gemm_topk", "moe_engine_save", "moe_engine_load_file",
+    "moe_engine_set_replica_split", "moe_engine_forward_dense",
 ]
 
 
@@ -75,6 +77,8 @@ def lib() -> C.CDLL:
             "moe_engine_set_expert_map": [_P, _P, _I64],
             "moe_route_gemm_topk": [_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _I32, _P, _P, _P, _P],
             "moe_engine_save": [_P, C.c_char_p],
+            "moe_engine_set_replica_split": [_P, _I32, _I32],
+            "moe_engine_forward_dense": [_P, _I64, _P, _P, _I64, _I32, _I32, _P],
             "moe_engine_load_file": [_P, C.c_char_p],
         }
         for name, args in sig.items():
@@ -144,6 +148,18 @@ class Engine:
     def forward_noalloc(self, x, y, ids, w, act_dtype, out_dtype, stream=None):
         call("moe_engine_forward_noalloc", self.h, x.data_ptr(), y.data_ptr(), ids.data_ptr(), w.data_ptr(),
              x.shape[0], ids.shape[1], act_dtype, out_dtype, stream_handle(stream))
+
+    def set_expert_map(self, local_of_global):
+        import numpy as np
+        m = np.ascontiguousarray(local_of_global, np.int32)
+        call("moe_engine_set_expert_map", self.h, m.ctypes.data, m.size)
+
+    def set_replica_split(self, rank, world):
+        call("moe_engine_set_replica_split", self.h, rank, world)
+
+    def forward_dense(self, expert, x, y, act_dtype, out_dtype, stream=None):
+        call("moe_engine_forward_dense", self.h, expert, x.data_ptr(), y.data_ptr(), x.shape[0], act_dtype, out_dtype,
+             stream_handle(stream))
 
     def save(self, path):
         call("moe_engine_save", self.h, os.fsencode(path))

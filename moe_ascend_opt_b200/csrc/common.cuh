@@ -31,8 +31,20 @@ MOE_DEV void set_err(int32_t* err, int32_t code) {
 // Global expert id -> this engine's local id, or -1 for experts it does not hold: through
 // the placement map when one is set (local_of_global[gid]), else the contiguous block
 // [e_off, e_off + E).  Invalid ids are skipped like in the reference (moe_common.cpp:158).
-MOE_DEV int local_expert(int gid, int e_off, int E, const int32_t* emap, int emap_n) {
-    if (emap) return (gid >= 0 && gid < emap_n) ? emap[gid] : -1;
+// A map entry with kReplicaFlag marks a hot expert replicated on every rank: this engine
+// takes the pair only when (token + gid) % world == rank, with world and rank stored after
+// the map's emap_n entries, so that every pair is computed by exactly one rank.
+constexpr int32_t kReplicaFlag = 1 << 30;
+MOE_DEV int local_expert(int gid, int e_off, int E, const int32_t* emap, int emap_n, int pair, int K) {
+    if (emap) {
+        if (gid < 0 || gid >= emap_n) return -1;
+        const int v = emap[gid];
+        if (v >= 0 && (v & kReplicaFlag)) {
+            const int world = emap[emap_n], rank = emap[emap_n + 1];
+            return ((pair / K + gid) % world == rank) ? (v & ~kReplicaFlag) : -1;
+        }
+        return v;
+    }
     const int g = gid - e_off;
     return (g >= 0 && g < E) ? g : -1;
 }

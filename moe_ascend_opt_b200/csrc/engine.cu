@@ -66,8 +66,12 @@ struct moe_engine {
     int cl_clusters[3] = {-1, -1, -1};  // co-resident clusters per format (-1: not queried)
     float* clpart = nullptr;  // its per-pair fp32 down rows [clpart_cap][H]
     int64_t clpart_cap = 0;
-    int32_t* emap = nullptr;  // optional placement map: global expert id -> local id or -1
+    int32_t* emap = nullptr;  // optional placement map: global expert id -> local id or -1 (+ replica split)
     int32_t emap_n = 0;
+    std::vector<int32_t> emap_host;  // the map as set (flags included)
+    int32_t rep_rank = 0, rep_world = 1;  // replicated experts: pairs with (token + id) % world == rank
+    void* dense_ids = nullptr;  // dense forward: routing ids [cap] (the expert) | weights [cap] (1.0)
+    int64_t dense_cap = 0, dense_expert = -1;
     int32_t sk_cost_a = 3;  // its chunk cost model: streaming share per chunk vs one token of compute
     int32_t sk_min_chunks_per_cta = 2;  // use it from this many (unique expert x I/32) chunks per CTA
     // expert-parallel combine over peer memory (moe_engine_p2p_mailbox / _connect)
@@ -1134,10 +1138,10 @@ int forward_gemm_awq(moe_engine* eng, const void* x, void* y, const int32_t* ids
     if (int rc = gemm_workspace(eng, T, K, w)) return rc;
     const int nblk = (TK + gemm::kChunk - 1) / gemm::kChunk;
     const int eoff = eng->cfg.expert_offset;
-    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk);
+    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, (int)K, E, eoff, eng->emap, eng->emap_n, w.blk);
     gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
                                                                                   w.mtile, gemm::kTcM);
-    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk, w.starts,
+    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, (int)K, E, eoff, eng->emap, eng->emap_n, w.blk, w.starts,
                                                        w.smap, w.tokmap);
     CUDA_TRY(cudaGetLastError());
     if (int rc = launch_gemms_tc<2>(eng, w, x, act_bf16, T, K, st)) return rc;
@@ -1216,10 +1220,10 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
     if (int rc = gemm_workspace(eng, T, K, w)) return rc;
     const int nblk = (TK + gemm::kChunk - 1) / gemm::kChunk;
     const int eoff = eng->cfg.expert_offset;
-    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk);
+    gemm::route_count_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, (int)K, E, eoff, eng->emap, eng->emap_n, w.blk);
     gemm::route_scan_kernel<<<1, std::max(32, (E + 31) / 32 * 32), 2 * E * 4, st>>>(w.blk, nblk, E, w.counts, w.starts,
                                                                                   w.mtile, std::abs(gemm_tile_rows(eng, TK)));
-    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, E, eoff, eng->emap, eng->emap_n, w.blk, w.starts,
+    gemm::route_place_kernel<<<nblk, 256, E * 4, st>>>(ids, TK, (int)K, E, eoff, eng->emap, eng->emap_n, w.blk, w.starts,
                                                        w.smap, w.tokmap);
     const int bm = gemm_tile_rows(eng, TK);
     if (bm == 128) {
@@ -1265,6 +1269,21 @@ int forward_gemm_t(moe_engine* eng, const void* x, void* y, const int32_t* ids, 
             w.out, w.smap, tw, (int)T, (int)K, H, y, out_kind);
         CUDA_TRY(cudaGetLastError());
     }
+    return MOE_OK;
+}
+
+// The placement map on the device: emap_n entries, then the replica split (world, rank).
+int upload_expert_map(moe_engine* eng) {
+    DeviceGuard g(eng->cfg.device);
+    CUDA_TRY(cudaDeviceSynchronize());  // the old map may still be read by queued work
+    if (eng->emap) CUDA_TRY(cudaFree(eng->emap));
+    eng->emap = nullptr;
+    std::vector<int32_t> m(eng->emap_host);
+    m.push_back(eng->rep_world);
+    m.push_back(eng->rep_rank);
+    CUDA_TRY(cudaMalloc(&eng->emap, m.size() * sizeof(int32_t)));
+    CUDA_TRY(cudaMemcpy(eng->emap, m.data(), m.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
+    eng->emap_n = (int32_t)eng->emap_host.size();
     return MOE_OK;
 }
 
@@ -1369,6 +1388,7 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     cudaFree(eng->agu);
     cudaFree(eng->adn);
     cudaFree(eng->clpart);
+    cudaFree(eng->dense_ids);
     cudaFree(eng->emap);
     cudaFree(eng->part);
     for (int q = 0; q < kMaxPeers; ++q)
@@ -1681,6 +1701,51 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         eng->timed = true;
     }
     return MOE_OK;
+}
+
+// Dense MLP through the same fused kernels: every token routed to one expert with weight 1.
+__global__ void fill_dense_route_kernel(int32_t* ids, float* w, int64_t n, int32_t expert) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        ids[i] = expert;
+        w[i] = 1.0f;
+    }
+}
+
+extern "C" int moe_engine_forward_dense(moe_engine* eng, int64_t expert, const void* x, void* y, int64_t T,
+                                        int32_t act_dtype, int32_t out_dtype, void* stream) {
+    if (int rc = check_engine(eng)) return rc;
+    if (expert < 0 || expert >= eng->cfg.num_experts) return fail(MOE_ERR_INVALID, "expert index out of range");
+    if (T < 0) return fail(MOE_ERR_INVALID, "num_tokens must be >= 0");
+    if (T == 0) return MOE_OK;
+    DeviceGuard g(eng->cfg.device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (T > eng->dense_cap) {
+        CUDA_TRY(cudaDeviceSynchronize());  // the old buffers may still be in use by queued work
+        cudaFree(eng->dense_ids);
+        eng->dense_ids = nullptr;
+        int64_t cap = std::max<int64_t>(64, eng->dense_cap);
+        while (cap < T) cap *= 2;
+        CUDA_TRY(cudaMalloc(&eng->dense_ids, (size_t)cap * 8));
+        eng->dense_cap = cap;
+        eng->dense_expert = -1;
+    }
+    int32_t* ids = reinterpret_cast<int32_t*>(eng->dense_ids);
+    float* w = reinterpret_cast<float*>(ids + eng->dense_cap);
+    // global id of the expert for the routing (placement map or contiguous block)
+    int32_t gid = (int32_t)(expert + eng->cfg.expert_offset);
+    if (!eng->emap_host.empty()) {
+        gid = -1;
+        for (size_t gg = 0; gg < eng->emap_host.size(); ++gg)
+            if (eng->emap_host[gg] >= 0 && (eng->emap_host[gg] & ~kReplicaFlag) == expert) gid = (int32_t)gg;
+        if (gid < 0) return fail(MOE_ERR_INVALID, "expert is not in this engine's placement map");
+    }
+    if (eng->dense_expert != gid) {  // (re)fill on the stream; stays valid for later calls
+        fill_dense_route_kernel<<<(unsigned)((eng->dense_cap + 255) / 256), 256, 0, st>>>(ids, w, eng->dense_cap, gid);
+        CUDA_TRY(cudaGetLastError());
+        eng->dense_expert = gid;
+    }
+    return moe_engine_forward(eng, x, y, ids, w, T, 1, act_dtype, out_dtype, stream);
 }
 
 extern "C" int moe_engine_last_time_ms(moe_engine* eng, double* ms) {
@@ -2106,16 +2171,20 @@ extern "C" int moe_engine_set_expert_map(moe_engine* eng, const int32_t* local_o
     const int64_t E = eng->cfg.num_experts;
     std::vector<int> seen(E, 0);
     for (int64_t g = 0; g < num_global; ++g) {
-        const int32_t l = local_of_global[g];
-        if (l == -1) continue;
-        if (l < 0 || l >= E || seen[l]++) return fail(MOE_ERR_INVALID, "expert map must send each local expert id once");
+        const int32_t v = local_of_global[g];
+        if (v == -1) continue;
+        const int32_t l = v & ~kReplicaFlag;
+        if (v < 0 || l >= E || seen[l]++) return fail(MOE_ERR_INVALID, "expert map must send each local expert id once");
     }
-    DeviceGuard g(eng->cfg.device);
-    CUDA_TRY(cudaDeviceSynchronize());  // the old map may still be read by queued work
-    if (eng->emap) CUDA_TRY(cudaFree(eng->emap));
-    eng->emap = nullptr;
-    CUDA_TRY(cudaMalloc(&eng->emap, (size_t)num_global * sizeof(int32_t)));
-    CUDA_TRY(cudaMemcpy(eng->emap, local_of_global, (size_t)num_global * sizeof(int32_t), cudaMemcpyHostToDevice));
-    eng->emap_n = (int32_t)num_global;
-    return MOE_OK;
+    eng->emap_host.assign(local_of_global, local_of_global + num_global);
+    return upload_expert_map(eng);
+}
+
+extern "C" int moe_engine_set_replica_split(moe_engine* eng, int32_t rank, int32_t world) {
+    if (int rc = check_engine(eng)) return rc;
+    if (world < 1 || rank < 0 || rank >= world) return fail(MOE_ERR_INVALID, "bad replica split rank / world");
+    eng->rep_rank = rank;
+    eng->rep_world = world;
+    if (eng->emap_host.empty()) return MOE_OK;  // applied when the map is set
+    return upload_expert_map(eng);
 }

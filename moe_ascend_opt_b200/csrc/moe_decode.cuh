@@ -181,7 +181,7 @@ MOE_DEV RouteSmem carve_route(int32_t* base, int TK, int E) {
 // Stable counting sort by one warp (moe_common.cpp:146-184): pairs are taken in
 // (t,k) order 32 at a time; lanes with the same expert rank themselves with
 // __match_any_sync, so positions inside an expert follow pair order exactly.
-MOE_DEV void route_warp(const int32_t* g_ids, int TK, int E, int e_off, const int32_t* emap, int emap_n, RouteSmem r,
+MOE_DEV void route_warp(const int32_t* g_ids, int TK, int K, int E, int e_off, const int32_t* emap, int emap_n, RouteSmem r,
                         int lane) {
     for (int e = lane; e < E; e += 32) r.cnt[e] = 0;
     __syncwarp();
@@ -189,7 +189,7 @@ MOE_DEV void route_warp(const int32_t* g_ids, int TK, int E, int e_off, const in
         const int i = i0 + lane;
         int e = -1;
         if (i < TK) {
-            e = local_expert(g_ids[i], e_off, E, emap, emap_n);
+            e = local_expert(g_ids[i], e_off, E, emap, emap_n, i, K);
             r.ids[i] = e;
         }
         const unsigned peers = __match_any_sync(0xffffffffu, e);
@@ -649,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_kernel(const DecodePar
     if (warp == kWarps - 1) {  // one warp routes while the others quantise the tokens
         // this launch's barrier target: the load is in flight while the warp routes
         const unsigned long long launch_idx = barrier_launch_index(p.bar, (uint32_t)G);
-        route_warp(p.ids, TK, E, p.e_off, p.emap, p.emap_n, rt, lane);
+        route_warp(p.ids, TK, p.K, E, p.e_off, p.emap, p.emap_n, rt, lane);
         if (lane == 0) {
             s_ok = 1;
             s_launch = launch_idx;

@@ -65,7 +65,7 @@ struct ClParams {
     void* y;
     const int32_t* ids;
     const float* tw;
-    float* part;         // [H][T*K*Q] fp32 partial down rows per routed pair and K-range
+    float* part;         // [T*K*Q][H] fp32 partial down rows per routed pair and K-range
     unsigned int* cnt;   // [kClRowBlocks] combine arrival counters (zero between launches)
     int32_t* err;
     int32_t qmask;       // allowed Q values (bit log2 Q)
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     if (lane == 0)
         for (int s = 0; s < kClInFlight; ++s) mbar_init(&mybar[s], 1);
     if (warp == kClWarps - 1) {
-        route_warp(p.ids, TK, E, p.e_off, p.emap, p.emap_n, rt, lane);
+        route_warp(p.ids, TK, p.K, E, p.e_off, p.emap, p.emap_n, rt, lane);
         // pieces: each expert in slices of at most T positions (one unless ids repeat inside a
         // token); lane l owns the contiguous experts [l cu, l cu + cu), a warp scan gives their
         // first piece
@@ -759,12 +759,10 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
             }
         }
         __syncthreads();
-        // the routed pairs' partials of this CTA's rows into `part` [H][T*K*Q]: the Q partials
-        // of every pair of an output element are contiguous for the combine
-        const int PQ = TK * Q;
+        // the routed pairs' partial rows of this CTA into `part` [(pos * Q + q)][H] (coalesced)
         for (int idx = tid; idx < mc * RPC; idx += kClThreads) {
             const int m = idx / RPC, r = idx - m * RPC;
-            __stcg(p.part + (size_t)(rank * RPC + r) * PQ + (ps + m) * Q + q, outs[idx]);
+            __stcg(p.part + ((size_t)(ps + m) * Q + q) * H + rank * RPC + r, outs[idx]);
         }
         __syncthreads();  // outs / hq are reused by the next work unit
     };
@@ -806,44 +804,39 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         return;
     }
     stamp(11);
-    // the completed blocks' elements, one per thread: for each routed pair in k order, its Q
-    // contiguous K-range partials (vector loads, the loads of 8 pairs in flight together),
-    // summed in a fixed order, weighted and accumulated in k order
-    const int nl = __popc(last), PQ = TK * Q;
+    // the completed blocks' elements, one per thread (consecutive threads: consecutive rows, so
+    // every load is coalesced): for each routed pair in k order, its Q K-range partials, all
+    // loads of 4 pairs in flight together, summed in q order, weighted and accumulated in k order
+    const int nl = __popc(last);
     for (int idx = tid; idx < nl * T * RB; idx += kClThreads) {
         const int bi = idx / (T * RB), rem = idx - bi * (T * RB);
         int b = 0;
         for (int seen = -1; ; ++b)
             if ((last >> b) & 1u) { if (++seen == bi) break; }
         const int t = rem / RB, n = (blk0 + b) * RB + rem % RB;
-        const float* row = p.part + (size_t)n * PQ;
         float acc = 0.f;
-        for (int k0 = 0; k0 < p.K; k0 += 8) {
-            // all loads of 8 pairs first (pairs without a position read a valid address and
-            // are dropped), then the sums in (k, q) order
-            float4 v[8];
-            int pos[8];
+        for (int k0 = 0; k0 < p.K; k0 += 4) {
+            int pos[4];
+            float v[4];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 4; ++j) {
                 pos[j] = k0 + j < p.K ? rt.smap[t * p.K + k0 + j] : -1;
-                v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                v[j] = 0.f;
             }
-            for (int i = 0; i < Q; i += 4) {
+            for (int q0 = 0; q0 < Q; q0 += 4) {
+                float a[4][4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float* src = row + (pos[j] >= 0 ? pos[j] : 0) * Q + i;
-                    if (Q >= 4) {
-                        const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
-                        v[j].x += a.x; v[j].y += a.y; v[j].z += a.z; v[j].w += a.w;
-                    } else {
-                        v[j].x += __ldcg(src);
-                        if (Q == 2) v[j].y += __ldcg(src + 1);
-                    }
-                }
+                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                    for (int qq = 0; qq < 4; ++qq)
+                        a[j][qq] = (pos[j] >= 0 && q0 + qq < Q)
+                                       ? __ldcg(p.part + ((size_t)pos[j] * Q + q0 + qq) * H + n) : 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[j] += ((a[j][0] + a[j][1]) + (a[j][2] + a[j][3]));
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (pos[j] >= 0) acc += p.tw[t * p.K + k0 + j] * ((v[j].x + v[j].y) + (v[j].z + v[j].w));
+            for (int j = 0; j < 4; ++j)
+                if (pos[j] >= 0) acc += p.tw[t * p.K + k0 + j] * v[j];
         }
         const size_t o = (size_t)t * H + n;
         if (p.out_kind == 2) reinterpret_cast<float*>(p.y)[o] = acc;

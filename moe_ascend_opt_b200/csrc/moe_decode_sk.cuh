@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_decode_sk_kernel(const Decode
     if (warp == kWarps - 1) {
         // this launch's barrier target: the load is in flight while the warp routes
         const unsigned long long launch_idx = barrier_launch_index(p.bar, (uint32_t)G);
-        route_warp(p.ids, TK, E, p.e_off, p.emap, p.emap_n, rt, lane);
+        route_warp(p.ids, TK, p.K, E, p.e_off, p.emap, p.emap_n, rt, lane);
         const int U = *rt.nuniq;
         int carry = 0;  // exclusive prefix of the chunk costs over the unique experts
         for (int u0 = 0; u0 < U; u0 += 32) {

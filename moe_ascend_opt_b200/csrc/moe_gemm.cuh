@@ -35,14 +35,14 @@ constexpr int kRowPad = 16;    // smem row padding (bank-conflict-free fragment 
 // Pairs are processed in chunks of kChunk by one CTA each.
 constexpr int kChunk = 1024;
 
-__global__ void route_count_kernel(const int32_t* ids, int TK, int E, int e_off, const int32_t* emap, int emap_n,
-                                   int32_t* blk_cnt) {
+__global__ void route_count_kernel(const int32_t* ids, int TK, int K, int E, int e_off, const int32_t* emap,
+                                   int emap_n, int32_t* blk_cnt) {
     extern __shared__ int32_t sh[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
     __syncthreads();
     const int base = blockIdx.x * kChunk;
     for (int i = threadIdx.x; i < kChunk && base + i < TK; i += blockDim.x) {
-        const int g = local_expert(ids[base + i], e_off, E, emap, emap_n);
+        const int g = local_expert(ids[base + i], e_off, E, emap, emap_n, base + i, K);
         if (g >= 0) atomicAdd(&sh[g], 1);
     }
     __syncthreads();
@@ -82,7 +82,7 @@ __global__ void route_scan_kernel(int32_t* blk_cnt, int nblk, int E, int32_t* co
 }
 
 // Stable positions: warp 0 walks the chunk 32 pairs at a time in (t,k) order.
-__global__ void route_place_kernel(const int32_t* ids, int TK, int E, int e_off, const int32_t* emap, int emap_n,
+__global__ void route_place_kernel(const int32_t* ids, int TK, int K, int E, int e_off, const int32_t* emap, int emap_n,
                                    const int32_t* blk_off,
                                    const int32_t* starts, int32_t* smap, int32_t* tokmap) {
     extern __shared__ int32_t run[];
@@ -95,7 +95,7 @@ __global__ void route_place_kernel(const int32_t* ids, int TK, int E, int e_off,
         const int i = base + i0 + lane;
         int e = -1;
         if (i < TK) {
-            e = local_expert(ids[i], e_off, E, emap, emap_n);
+            e = local_expert(ids[i], e_off, E, emap, emap_n, i, K);
         }
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(peers & ((1u << lane) - 1u));

@@ -15,13 +15,15 @@
 //   torch.ops.nanovllm.moe_forward_npu_graph_out(..., ctx, out)            :406
 //   torch.classes.nanovllm.MoEGraphContext(moe, num_tokens, top_k, dtype)  :398-399
 //   torch.classes.nanovllm.NpuCallbackManager(stream_ptr, device_id)       :395-396 (no-op)
-//   new: moe_forward_partial, moe_route, moe_route_gemm, moe_route_permute, quantize_rows_q8_0
+//   new: moe_forward_partial, moe_dense_forward, moe_route, moe_route_gemm, moe_route_permute,
+//        quantize_rows_q8_0
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/custom_class.h>
 #include <torch/library.h>
 #include <torch/torch.h>
 
+#include <algorithm>
 #include <string>
 
 #include "../../include/moe_b200.h"
@@ -47,6 +49,7 @@ struct MoEInferHandle : torch::CustomClassHolder {
     int64_t group_size = 128;
     int64_t ep_rank = 0, ep_size = 1;
     std::vector<int64_t> placement;  // global ids of the experts held here, in local order (empty: contiguous block)
+    std::vector<int64_t> replicas;   // hot experts held by every rank (a subset of placement)
     moe_engine* eng = nullptr;
     int device = -1;
 
@@ -78,9 +81,18 @@ struct MoEInferHandle : torch::CustomClassHolder {
         placement = experts;
     }
 
+    void set_expert_replicas(const std::vector<int64_t>& hot) {
+        TORCH_CHECK(!eng, "set_expert_replicas must precede weight loading");
+        TORCH_CHECK(!placement.empty(), "set_expert_placement (including the replicated experts) first");
+        for (int64_t e : hot)
+            TORCH_CHECK(std::find(placement.begin(), placement.end(), e) != placement.end(),
+                        "replicated expert ", e, " is not in this rank's placement");
+        replicas = hot;
+    }
+
     void set_expert_parallel(int64_t rank, int64_t size) {
         TORCH_CHECK(!eng, "set_expert_parallel must precede weight loading");
-        TORCH_CHECK(size >= 1 && rank >= 0 && rank < size && E % size == 0, "bad expert-parallel config");
+        TORCH_CHECK(size >= 1 && rank >= 0 && rank < size, "bad expert-parallel config");
         ep_rank = rank;
         ep_size = size;
     }
@@ -91,6 +103,8 @@ struct MoEInferHandle : torch::CustomClassHolder {
 
     void ensure_engine() {
         if (eng) return;
+        TORCH_CHECK(!placement.empty() || E % ep_size == 0,
+                    "bad expert-parallel config: contiguous expert blocks need E divisible by the world size");
         device = at::cuda::current_device();
         moe_config cfg{};
         cfg.num_experts = local_experts();
@@ -104,6 +118,8 @@ struct MoEInferHandle : torch::CustomClassHolder {
         if (!placement.empty()) {
             std::vector<int32_t> m(E, -1);
             for (size_t l = 0; l < placement.size(); ++l) m[placement[l]] = (int32_t)l;
+            for (int64_t e : replicas) m[e] |= MOE_REPLICATED;
+            check_rc(moe_engine_set_replica_split(eng, (int32_t)ep_rank, (int32_t)ep_size), "set_expert_replicas");
             check_rc(moe_engine_set_expert_map(eng, m.data(), E), "set_expert_placement");
         }
     }
@@ -284,6 +300,23 @@ at::Tensor moe_forward(const at::Tensor& hidden, const at::Tensor& ids, const at
     return out;
 }
 
+at::Tensor moe_dense_forward(const at::Tensor& hidden, int64_t expert, const c10::intrusive_ptr<MoEInferHandle>& moe) {
+    TORCH_CHECK(moe->eng, "no weights loaded");
+    TORCH_CHECK(hidden.is_cuda() && hidden.dim() == 2 && hidden.size(1) == moe->H && hidden.is_contiguous(),
+                "hidden must be a contiguous CUDA [T, H] tensor");
+    TORCH_CHECK(hidden.scalar_type() == at::kHalf || hidden.scalar_type() == at::kBFloat16,
+                "hidden must be float16 or bfloat16");
+    c10::cuda::CUDAGuard g(moe->device);
+    auto out = at::empty_like(hidden);
+    const int64_t le = moe->local_of(expert);
+    TORCH_CHECK(le >= 0, "expert ", expert, " is not held by this rank");
+    check_rc(moe_engine_forward_dense(moe->eng, le, hidden.data_ptr(), out.data_ptr(), hidden.size(0),
+                                      dtype_code(hidden.scalar_type()), dtype_code(out.scalar_type()),
+                                      cur_stream(moe->device)),
+             "moe_dense_forward");
+    return out;
+}
+
 at::Tensor moe_forward_partial(const at::Tensor& hidden, const at::Tensor& ids, const at::Tensor& w,
                                const c10::intrusive_ptr<MoEInferHandle>& moe) {
     auto out = at::empty(hidden.sizes(), hidden.options().dtype(at::kFloat));
@@ -364,6 +397,7 @@ TORCH_LIBRARY_FRAGMENT(nanovllm, m) {
         .def("store_awq", &MoEInferHandle::store_awq)
         .def("set_expert_parallel", &MoEInferHandle::set_expert_parallel)
         .def("set_expert_placement", &MoEInferHandle::set_expert_placement)
+        .def("set_expert_replicas", &MoEInferHandle::set_expert_replicas)
         .def("engine_handle",  // the moe_engine* behind this handle, for direct C-ABI calls (include/moe_b200.h)
              [](const c10::intrusive_ptr<MoEInferHandle>& s) -> int64_t {
                  TORCH_CHECK(s->eng, "no weights loaded");
@@ -422,6 +456,7 @@ TORCH_LIBRARY_FRAGMENT(nanovllm, m) {
     m.def("moe_forward_npu_graph_out(Tensor hidden, Tensor topk_ids, Tensor topk_w, __torch__.torch.classes.nanovllm.MoEInfer moe, __torch__.torch.classes.nanovllm.MoEGraphContext ctx, Tensor(a!) out) -> ()");
     m.def("moe_forward_partial(Tensor hidden, Tensor topk_ids, Tensor topk_w, __torch__.torch.classes.nanovllm.MoEInfer moe) -> Tensor");
     m.def("moe_route(Tensor logits, int top_k, bool renormalize) -> (Tensor, Tensor)");
+    m.def("moe_dense_forward(Tensor hidden, int expert, __torch__.torch.classes.nanovllm.MoEInfer moe) -> Tensor");
     m.def("moe_route_gemm(Tensor hidden, Tensor router_weight, int top_k, bool renormalize) -> (Tensor, Tensor)");
     m.def("moe_route_permute(Tensor topk_ids, int num_experts) -> (Tensor, Tensor, Tensor, Tensor)");
     m.def("quantize_rows_q8_0(Tensor x) -> (Tensor, Tensor)");
@@ -433,6 +468,7 @@ TORCH_LIBRARY_IMPL(nanovllm, CUDA, m) {
     m.impl("moe_forward_npu_graph_out", &moe_forward_graph_out);
     m.impl("moe_forward_partial", &moe_forward_partial);
     m.impl("moe_route", &moe_route);
+    m.impl("moe_dense_forward", &moe_dense_forward);
     m.impl("moe_route_gemm", &moe_route_gemm);
     m.impl("moe_route_permute", &route_permute);
     m.impl("quantize_rows_q8_0", &quantize_rows);

@@ -49,10 +49,32 @@ def balanced_placement(load, world: int) -> List[List[int]]:
     return [sorted(r) for r in ranks]
 
 
-def placement_imbalance(load, placement: List[List[int]]) -> float:
-    """max / mean of the per-rank load (1.0 = perfectly balanced)."""
+def replicated_placement(load, world: int, n_hot: int) -> Tuple[List[List[int]], List[int]]:
+    """Hot-expert replication: the n_hot most loaded experts are held by every rank (their
+    routed pairs are split between the ranks by token: (t + e) % world), the others are dealt
+    by balanced_placement.  Returns (per-rank expert lists, replicated experts); each rank's
+    list holds its own experts followed by the replicated ones.  The rest (E - n_hot) must
+    divide by the world size."""
     load = np.asarray(load, np.float64)
-    per_rank = np.array([load[r].sum() for r in placement])
+    E = load.shape[0]
+    if n_hot <= 0:
+        return balanced_placement(load, world), []
+    hot = [int(e) for e in np.argsort(-load, kind="stable")[:n_hot]]
+    rest = [e for e in range(E) if e not in set(hot)]
+    if len(rest) % world != 0:
+        raise ValueError(f"{len(rest)} experts outside the replicated set do not divide by {world} ranks")
+    sub = balanced_placement(load[rest], world)
+    ranks = [sorted(rest[i] for i in r) + sorted(hot) for r in sub]
+    return ranks, sorted(hot)
+
+
+def placement_imbalance(load, placement: List[List[int]], replicas: Optional[List[int]] = None) -> float:
+    """max / mean of the per-rank load (1.0 = perfectly balanced); a replicated expert's load
+    is split evenly over the ranks."""
+    load = np.asarray(load, np.float64)
+    rep = set(replicas or [])
+    W = len(placement)
+    per_rank = np.array([sum(load[e] / W if e in rep else load[e] for e in r) for r in placement])
     return float(per_rank.max() / max(per_rank.mean(), 1e-12))
 
 
@@ -80,7 +102,8 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, num_experts: int, hidden: int, inter: int, quant_type: int, group=None,
-                 group_size: int = 128, placement: Optional[List[List[int]]] = None):
+                 group_size: int = 128, placement: Optional[List[List[int]]] = None,
+                 replicas: Optional[List[int]] = None):
         import torch
         import torch.distributed as dist
 
@@ -98,6 +121,8 @@ class ExpertParallelMoE:
             if len(placement) != self.world:
                 raise ValueError("placement needs one expert list per rank")
             self.handle.set_expert_placement(list(placement[self.rank]))
+            if replicas:  # hot experts on every rank, e.g. from replicated_placement
+                self.handle.set_expert_replicas(list(replicas))
 
     def load_quantized(self, gate_up_qs, gate_up_d, down_qs, down_d):
         self.handle.store_quantized_repack(gate_up_qs, gate_up_d, down_qs, down_d)

@@ -125,3 +125,44 @@ def test_placed_partials_sum_to_full_forward(qt):
     total = sum(O.moe_forward_q(qt, False, xf, local_ids_map(ids, ex), w, gq[ex], gd[ex], dq[ex], dd[ex]) for ex in pl)
     full = O.moe_forward_q(qt, False, xf, ids, w, gq, gd, dq, dd)
     assert float(np.abs(total - full).max() / np.abs(full).max()) < 1e-5
+
+
+def test_replicated_placement_evens_zipf_load():
+    """Replicating the hottest experts on every rank removes the floor that one hot expert
+    puts under the balanced placement's imbalance."""
+    from moe_ascend_opt_b200.ep import balanced_placement, placement_imbalance, replicated_placement
+    E, W = 128, 8
+    load = 1.0 / np.arange(1, E + 1) ** 1.2
+    load = load[np.random.default_rng(3).permutation(E)]
+    pl, hot = replicated_placement(load, W, 8)
+    assert len(hot) == 8 and all(set(hot) <= set(r) for r in pl)
+    own = [e for r in pl for e in r if e not in hot]
+    assert sorted(own + hot) == list(range(E))
+    assert placement_imbalance(load, pl, hot) < 1.1 < placement_imbalance(load, balanced_placement(load, W))
+
+
+def replica_local_ids(ids, experts, hot, rank, world):
+    """The kernels' rule for a rank holding `experts` (local order) with replicated `hot`:
+    a pair of a hot expert g is this rank's when (t + g) % world == rank."""
+    from moe_ascend_opt_b200.ep import local_ids_map
+    loc = local_ids_map(ids, experts)
+    t = np.arange(ids.shape[0])[:, None]
+    mine = ((t + ids) % world) == rank
+    is_hot = np.isin(ids, hot)
+    return np.where(is_hot & ~mine, -1, loc).astype(np.int32)
+
+
+@pytest.mark.parametrize("qt", [0, 1])
+def test_replicated_partials_sum_to_full_forward(qt):
+    from oracle import oracle as O
+    from moe_ascend_opt_b200.ep import replicated_placement
+    from tests.helpers import q_weights, tokens
+    E, H, I, T, K, W = 16, 256, 128, 9, 4, 2
+    gq, gd, dq, dd = q_weights(qt, E, H, I, 19)
+    _, xf, ids, w = tokens(T, H, E, K, 19)
+    load = np.bincount(ids.ravel(), minlength=E)
+    pl, hot = replicated_placement(load, W, 2)
+    total = sum(O.moe_forward_q(qt, False, xf, replica_local_ids(ids, ex, hot, r, W), w, gq[ex], gd[ex], dq[ex],
+                                dd[ex]) for r, ex in enumerate(pl))
+    full = O.moe_forward_q(qt, False, xf, ids, w, gq, gd, dq, dd)
+    assert float(np.abs(total - full).max() / np.abs(full).max()) < 1e-5

@@ -149,3 +149,41 @@ def test_expert_placement_partials_on_one_gpu(T):
     y_ref = O.moe_forward_q(1, False, xf, ids, w, gq, gd, dq, dd)
     rel = float(np.abs(total.cpu().numpy() - y_ref).max() / np.abs(y_ref).max())
     assert rel <= 1e-2, rel
+
+
+@pytest.mark.parametrize("T,cl", [(1, "0"), (1, "8"), (5, "0"), (5, "8"), (64, "0")])
+def test_replicated_hot_experts_on_one_gpu(T, cl):
+    """Engines of 3 ranks on one GPU with 2 hot experts replicated on all of them: the fp32
+    partials sum to the full layer (decode kernels, cluster kernel, grouped GEMMs)."""
+    import os
+    from moe_ascend_opt_b200.ep import replicated_placement
+    from tests.helpers import q_weights, tokens
+    E, H, I, K, W = 32, 1024, 512, 8, 3
+    gq, gd, dq, dd = q_weights(1, E, H, I, 29)
+    xb, xf, ids, w = tokens(T, H, E, K, 29)
+    load = np.bincount(ids.ravel(), minlength=E)
+    pl, hot = replicated_placement(load, W, 2)
+    x = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+    old = os.environ.get("MOE_CL_MAX_TOKENS")
+    os.environ["MOE_CL_MAX_TOKENS"] = cl
+    total = None
+    try:
+        for r in range(W):
+            h = torch.classes.nanovllm.MoEInfer(E, H, I, 1)
+            h.set_expert_parallel(r, W)
+            h.set_expert_placement(pl[r])
+            h.set_expert_replicas(hot)
+            h.store_quantized_repack(torch.from_numpy(gq), torch.from_numpy(gd.view(np.int16)).view(torch.float16),
+                                     torch.from_numpy(dq), torch.from_numpy(dd.view(np.int16)).view(torch.float16))
+            part = torch.ops.nanovllm.moe_forward_partial(x, torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), h)
+            torch.cuda.synchronize()
+            assert h.device_error() == 0
+            total = part if total is None else total + part
+    finally:
+        if old is None:
+            del os.environ["MOE_CL_MAX_TOKENS"]
+        else:
+            os.environ["MOE_CL_MAX_TOKENS"] = old
+    y_ref = O.moe_forward_q(1, False, xf, ids, w, gq, gd, dq, dd)
+    rel = float(np.abs(total.cpu().numpy() - y_ref).max() / np.abs(y_ref).max())
+    assert rel <= 1e-2, rel
