@@ -63,5 +63,14 @@ def test_no_cpu_fallback():
 def test_expert_parallel_config_checks():
     h = torch.classes.nanovllm.MoEInfer(8, 256, 128, 0)
     with pytest.raises(RuntimeError, match="bad expert-parallel config"):
-        h.set_expert_parallel(0, 3)
+        h.set_expert_parallel(2, 2)
+    # 8 experts in contiguous blocks do not split over 3 ranks (a placement with replicated
+    # experts may); refused when the weights arrive
+    h3 = torch.classes.nanovllm.MoEInfer(8, 256, 128, 0)
+    h3.set_expert_parallel(0, 3)
+    with pytest.raises(RuntimeError, match="bad expert-parallel config"):
+        h3.store_quantized_repack(torch.zeros((8, 256, 256), dtype=torch.int8),
+                                  torch.zeros((8, 256, 8), dtype=torch.float16),
+                                  torch.zeros((8, 256, 128), dtype=torch.int8),
+                                  torch.zeros((8, 256, 4), dtype=torch.float16))
     h.set_expert_parallel(1, 2)
