@@ -63,6 +63,7 @@ struct moe_engine {
     uint8_t* adn = nullptr;
     int cl_max_tokens = -1;  // cluster decode kernel (moe_decode_cl_kernel) up to this many tokens (-1: by format)
     int cl_size = 4;         // its CTAs per cluster
+    bool pdl = true;         // launch it with programmatic stream serialization
     int cl_clusters[3] = {-1, -1, -1};  // co-resident clusters per format (-1: not queried)
     float* clpart = nullptr;  // its per-pair fp32 down rows [clpart_cap][H]
     int64_t clpart_cap = 0;
@@ -976,17 +977,21 @@ int launch_decode_cl(moe_engine* eng, ClPlan& pl, cudaStream_t st) {
     if (int rc = setup_decode_cl<FMT, XBF>(eng)) return rc;
     if (eng->cl_clusters[FMT] < 1) return fail(MOE_ERR_STATE, "no thread-block cluster fits");
     cudaLaunchConfig_t cfg{};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = eng->cl_size;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // programmatic dependent launch: the kernel waits (griddepcontrol.wait) for its stream
+    // predecessor before reading, so it may be scheduled while that one finishes
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(eng->cl_size * eng->cl_clusters[FMT]);
     cfg.blockDim = dim3(kClThreads);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = st;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = eng->pdl ? 2 : 1;
     CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_decode_cl_kernel<FMT, XBF>, pl.p));
     return MOE_OK;
 }
@@ -1358,6 +1363,7 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     }
     if (const char* v = std::getenv("MOE_DECODE_SK")) eng->use_sk = std::atoi(v) != 0;
     if (const char* v = std::getenv("MOE_CL_MAX_TOKENS")) eng->cl_max_tokens = std::atoi(v);
+    if (const char* v = std::getenv("MOE_PDL")) eng->pdl = std::atoi(v) != 0;
     if (const char* v = std::getenv("MOE_CL_SIZE")) {
         const int c = std::atoi(v);
         if (c == 1 || c == 2 || c == 4 || c == 8) eng->cl_size = c;
@@ -1365,7 +1371,7 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (const char* v = std::getenv("MOE_SK_COST_A")) eng->sk_cost_a = std::max(0, std::atoi(v));
     if (const char* v = std::getenv("MOE_SK_MIN_CHUNKS")) eng->sk_min_chunks_per_cta = std::max(0, std::atoi(v));
     eng->max_smem = (int)prop.sharedMemPerBlockOptin;
-    if (eng->cl_max_tokens < 0) eng->cl_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 0;  // where it is faster
+    if (eng->cl_max_tokens < 0) eng->cl_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 1;  // where it is faster
     int rc = MOE_OK;
     rc = alloc_q_layout(eng);
     if (rc == MOE_OK) rc = ensure_workspace(eng, 64);

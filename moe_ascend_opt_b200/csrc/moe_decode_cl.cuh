@@ -370,6 +370,11 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     if (tid == 0) s_last = 0u;
     if (lane == 0)
         for (int s = 0; s < kClInFlight; ++s) mbar_init(&mybar[s], 1);
+    // Programmatic dependent launch: the next kernel on the stream may be scheduled now (it
+    // waits for this grid's completion before it reads anything); this grid waits here for
+    // the kernel before it, which may have written the inputs, before its first read.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (warp == kClWarps - 1) {
         route_warp(p.ids, TK, p.K, E, p.e_off, p.emap, p.emap_n, rt, lane);
         // pieces: each expert in slices of at most T positions (one unless ids repeat inside a
