@@ -64,6 +64,10 @@ struct moe_engine {
     int cl_max_tokens = -1;  // cluster decode kernel (moe_decode_cl_kernel) up to this many tokens (-1: by format)
     int cl_size = 4;         // its CTAs per cluster
     bool pdl = true;         // launch it with programmatic stream serialization
+    int cl_combine = -1;     // its combine: 0 last arrivers in the kernel, 1 a separate kernel, -1 by T (> 1: kernel)
+    int64_t cl_item_bytes = 6144;  // target bytes of one bulk copy of its weight streams
+    int32_t* clmeta = nullptr;       // that kernel's input: Q | scatter map [clmeta_cap]
+    int64_t clmeta_cap = 0;
     int cl_clusters[3] = {-1, -1, -1};  // co-resident clusters per format (-1: not queried)
     float* clpart = nullptr;  // its per-pair fp32 down rows [clpart_cap][H]
     int64_t clpart_cap = 0;
@@ -909,14 +913,14 @@ bool plan_decode_cl(const moe_engine* eng, int T, int K, ClPlan& pl) {
     // ring items of up to ~6 KB
     int64_t maxitem;
     if (awq) {
-        p.upi = 10;  // gate_up records per item (5.6 KB)
-        p.kpi = 5;   // down records per item (5.6 KB)
+        p.upi = (int)std::max<int64_t>(1, eng->cl_item_bytes / kAwqGuRec);  // gate_up records per item
+        p.kpi = (int)std::max<int64_t>(1, eng->cl_item_bytes / kAwqDnRec);  // down records per item
         maxitem = std::max((int64_t)p.upi * kAwqGuRec, (int64_t)p.kpi * kAwqDnRec);
     } else {
         const int BB = qt == MOE_Q4_0 ? 16 : 32;
         const int64_t ub = eng->unit_bytes(), SBq = 32 * BB + 64;
-        p.upi = (int)std::max<int64_t>(1, 6144 / ub);
-        p.kpi = (int)std::max<int64_t>(1, 6144 / SBq);
+        p.upi = (int)std::max<int64_t>(1, eng->cl_item_bytes / ub);
+        p.kpi = (int)std::max<int64_t>(1, eng->cl_item_bytes / SBq);
         maxitem = std::max((int64_t)p.upi * ub, (int64_t)p.kpi * SBq);
     }
     off = round_up(off + 12 * kClWarps * kClInFlight, 128);  // mbarriers and item offsets
@@ -993,6 +997,17 @@ int launch_decode_cl(moe_engine* eng, ClPlan& pl, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = eng->pdl ? 2 : 1;
     CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_decode_cl_kernel<FMT, XBF>, pl.p));
+    if (pl.p.meta) {
+        const int n = pl.p.T * pl.p.H;
+        cudaLaunchConfig_t c2{};
+        c2.gridDim = dim3((n + 255) / 256);
+        c2.blockDim = dim3(256);
+        c2.stream = st;
+        c2.attrs = attr + 1;
+        c2.numAttrs = eng->pdl ? 1 : 0;
+        CUDA_TRY(cudaLaunchKernelEx(&c2, cl_combine_kernel, (const float*)pl.p.part, (const int32_t*)pl.p.meta,
+                                    pl.p.tw, pl.p.T, pl.p.K, pl.p.H, pl.p.y, pl.p.out_kind));
+    }
     return MOE_OK;
 }
 
@@ -1364,6 +1379,8 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (const char* v = std::getenv("MOE_DECODE_SK")) eng->use_sk = std::atoi(v) != 0;
     if (const char* v = std::getenv("MOE_CL_MAX_TOKENS")) eng->cl_max_tokens = std::atoi(v);
     if (const char* v = std::getenv("MOE_PDL")) eng->pdl = std::atoi(v) != 0;
+    if (const char* v = std::getenv("MOE_CL_COMBINE")) eng->cl_combine = std::strcmp(v, "kernel") == 0 ? 1 : 0;
+    if (const char* v = std::getenv("MOE_CL_ITEM_BYTES")) eng->cl_item_bytes = std::max(512, std::atoi(v));
     if (const char* v = std::getenv("MOE_CL_SIZE")) {
         const int c = std::atoi(v);
         if (c == 1 || c == 2 || c == 4 || c == 8) eng->cl_size = c;
@@ -1395,6 +1412,7 @@ extern "C" int moe_engine_destroy(moe_engine* eng) {
     cudaFree(eng->adn);
     cudaFree(eng->clpart);
     cudaFree(eng->dense_ids);
+    cudaFree(eng->clmeta);
     cudaFree(eng->emap);
     cudaFree(eng->part);
     for (int q = 0; q < kMaxPeers; ++q)
@@ -1550,6 +1568,12 @@ extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t t
     if (eng->dk)
         if (int rc = ensure_part(eng, std::min<int64_t>(max_tokens, 64))) return rc;
     if (int rc = ensure_clpart(eng, std::min<int64_t>(max_tokens, 8) * top_k * kClMaxQ)) return rc;
+    if (eng->cl_combine != 0 && 1 + std::min<int64_t>(max_tokens, 8) * top_k > eng->clmeta_cap) {
+        cudaFree(eng->clmeta);
+        eng->clmeta = nullptr;
+        eng->clmeta_cap = 1 + std::min<int64_t>(max_tokens, 8) * top_k;
+        CUDA_TRY(cudaMalloc(&eng->clmeta, (size_t)eng->clmeta_cap * 4));
+    }
     return ensure_workspace(eng, std::min<int64_t>(max_tokens, 64) * top_k);
 }
 
@@ -1645,6 +1669,16 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
             p.dn = eng->adn;
             p.part = eng->clpart;
             p.cnt = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(eng->bar) + 128);
+            if (eng->cl_combine == 1 || (eng->cl_combine < 0 && T > 1)) {
+                if (1 + T * K > eng->clmeta_cap) {
+                    CUDA_TRY(cudaDeviceSynchronize());
+                    cudaFree(eng->clmeta);
+                    eng->clmeta = nullptr;
+                    eng->clmeta_cap = std::max<int64_t>(1 + T * K, 1 + 8 * 64);
+                    CUDA_TRY(cudaMalloc(&eng->clmeta, (size_t)eng->clmeta_cap * 4));
+                }
+                p.meta = eng->clmeta;
+            }
             p.err = eng->err;
             p.dbg = eng->timeline;
             const int rc = qt == MOE_Q4_0 ? launch_decode_cl<kQ4, true>(eng, cp, st)
@@ -1729,6 +1763,7 @@ extern "C" int moe_engine_forward_dense(moe_engine* eng, int64_t expert, const v
     if (T > eng->dense_cap) {
         CUDA_TRY(cudaDeviceSynchronize());  // the old buffers may still be in use by queued work
         cudaFree(eng->dense_ids);
+    cudaFree(eng->clmeta);
         eng->dense_ids = nullptr;
         int64_t cap = std::max<int64_t>(64, eng->dense_cap);
         while (cap < T) cap *= 2;

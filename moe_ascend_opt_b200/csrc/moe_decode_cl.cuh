@@ -69,6 +69,7 @@ struct ClParams {
     unsigned int* cnt;   // [kClRowBlocks] combine arrival counters (zero between launches)
     int32_t* err;
     int32_t qmask;       // allowed Q values (bit log2 Q)
+    int32_t* meta;       // separate-combine mode (non-null): Q, then the routing's scatter map [T*K]
     // shared-memory carve-up (bytes)
     int32_t off_wl, off_x, off_h, off_hq, off_p, off_out, off_ring;
     int32_t ring_bytes;  // per-warp byte ring (items of different sizes, up to kClInFlight in flight)
@@ -445,8 +446,12 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     const int NW = s_nwu, Q = s_q;
     const int n_my = cid < NW ? (NW - cid + NC - 1) / NC : 0;
 
+    if (p.meta && cid == 0 && rank == 0) {  // the separate combine kernel reads Q and the scatter map
+        if (tid == 0) p.meta[0] = Q;
+        for (int i = tid; i < TK; i += kClThreads) p.meta[1 + i] = rt.smap[i];
+    }
     if (NW == 0) {  // no routed pair on this engine: the output is zero (q8_gemm.cpp:328-333)
-        if (cid == 0)
+        if (cid == 0 && !p.meta)
             for (int idx = tid; idx < T * RPC; idx += kClThreads) {
                 const int t = idx / RPC, n = rank * RPC + idx % RPC;
                 const size_t o = (size_t)t * H + n;
@@ -792,6 +797,10 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         for (int i = consumed; i < W.nissued; ++i) mbar_wait(&mybar[i % kClInFlight], (uint32_t)(i / kClInFlight) & 1u);
 
     // ---------------- combine ----------------
+    if (p.meta) {  // the combine runs as its own kernel (cl_combine_kernel) after this grid
+        flush_stamps();
+        return;
+    }
     const int RB = H / kClRowBlocks;                // rows per combine block
     const int nblk = RPC / RB, blk0 = rank * nblk;  // this CTA's blocks
     // the CTA barrier orders every thread's partial stores before the counter updates, whose
@@ -851,6 +860,48 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     if (tid < nblk && ((last >> tid) & 1u)) p.cnt[blk0 + tid] = 0u;  // the next launch starts from zero
     stamp(9);
     flush_stamps();
+}
+
+// The combine as a kernel of its own (launched right after moe_decode_cl_kernel, with
+// programmatic dependent launch): one thread per output element (t, n), consecutive threads on
+// consecutive rows (coalesced); for each routed pair in k order its Q K-range partials, summed
+// in q order, weighted, accumulated in k order and cast (q8_gemm.cpp:593-641).  Deterministic.
+__global__ void __launch_bounds__(256) cl_combine_kernel(const float* part, const int32_t* meta, const float* tw,
+                                                         int T, int K, int H, void* y, int out_kind) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid has completed
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= T * H) return;
+    const int t = idx / H, n = idx - t * H;
+    const int Q = __ldcg(meta);
+    const int32_t* smap = meta + 1;
+    float acc = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 4) {
+        int pos[4];
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            pos[j] = k0 + j < K ? __ldcg(smap + t * K + k0 + j) : -1;
+            v[j] = 0.f;
+        }
+        for (int q0 = 0; q0 < Q; q0 += 4) {
+            float a[4][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq)
+                    a[j][qq] = (pos[j] >= 0 && q0 + qq < Q) ? __ldcg(part + ((size_t)pos[j] * Q + q0 + qq) * H + n) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] += ((a[j][0] + a[j][1]) + (a[j][2] + a[j][3]));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (pos[j] >= 0) acc += tw[t * K + k0 + j] * v[j];
+    }
+    const size_t o = (size_t)t * H + n;
+    if (out_kind == 2) reinterpret_cast<float*>(y)[o] = acc;
+    else if (out_kind == 1) reinterpret_cast<__nv_bfloat16*>(y)[o] = __float2bfloat16_rn(acc);
+    else reinterpret_cast<__half*>(y)[o] = __float2half_rn(acc);
 }
 
 }  // namespace moe
