@@ -14,6 +14,7 @@
 #include "../../include/moe_b200.h"
 #include "common.cuh"
 #include "moe_decode_cl.cuh"
+#include "moe_decode_tp.cuh"
 #include "moe_decode_sk.cuh"
 #include "moe_gemm_tc.cuh"
 
@@ -61,6 +62,7 @@ struct moe_engine {
     // down [E][H/32][I/64] (adn); Q8_0 / Q4_0 down row slices [E][H/32][I/32] (adn)
     uint8_t* agu = nullptr;
     uint8_t* adn = nullptr;
+    int tp_max_tokens = -1;  // two-pass decode kernels (tp_gate_up / tp_down) up to this many tokens (-1: by format)
     int cl_max_tokens = -1;  // cluster decode kernel (moe_decode_cl_kernel) up to this many tokens (-1: by format)
     int cl_size = 4;         // its CTAs per cluster
     bool pdl = true;         // launch it with programmatic stream serialization
@@ -537,10 +539,14 @@ __global__ void awq_pack_sz_kernel(uint8_t* base, const uint16_t* sc, const int3
     r[soff + 2 * ng + g] = (uint8_t)awq_nib(qz + e * ng * (N / 8), g, N, n);
 }
 
+// Device counters: the grid barrier and the cluster kernel's combine counters in the first
+// 256 bytes, the two-pass kernels' row-block counters [H/32] after them.
+size_t bar_bytes(const moe_engine* eng) { return 256 + (size_t)(eng->cfg.hidden_size / 32 + 1) * 4; }
+
 int ensure_workspace(moe_engine* eng, int64_t positions) {
     if (!eng->bar) {
-        CUDA_TRY(cudaMalloc(&eng->bar, 256));
-        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
+        CUDA_TRY(cudaMalloc(&eng->bar, bar_bytes(eng)));
+        CUDA_TRY(cudaMemset(eng->bar, 0, bar_bytes(eng)));
     }
     if (!eng->herr) {
         CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&eng->herr), 64, cudaHostAllocMapped));
@@ -942,7 +948,7 @@ bool plan_decode_cl(const moe_engine* eng, int T, int K, ClPlan& pl) {
 
 template <int FMT, bool XBF>
 int setup_decode_cl(moe_engine* eng) {
-    auto kern = moe_decode_cl_kernel<FMT, XBF>;
+    auto kern = moe_decode_cl_kernel<FMT, XBF, 0>;
     static thread_local bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -950,6 +956,8 @@ int setup_decode_cl(moe_engine* eng) {
     const int dyn = eng->max_smem - 1024;
     if (dev >= 64 || !attr_set[dev]) {
         CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+        CUDA_TRY(cudaFuncSetAttribute(moe_decode_cl_kernel<FMT, XBF, 1>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
         if (dev < 64) attr_set[dev] = true;
     }
     int& nc = eng->cl_clusters[FMT];
@@ -996,7 +1004,8 @@ int launch_decode_cl(moe_engine* eng, ClPlan& pl, cudaStream_t st) {
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = eng->pdl ? 2 : 1;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_decode_cl_kernel<FMT, XBF>, pl.p));
+    if (pl.p.T == 1) CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_decode_cl_kernel<FMT, XBF, 1>, pl.p));
+    else CUDA_TRY(cudaLaunchKernelEx(&cfg, moe_decode_cl_kernel<FMT, XBF, 0>, pl.p));
     if (pl.p.meta) {
         const int n = pl.p.T * pl.p.H;
         cudaLaunchConfig_t c2{};
@@ -1331,7 +1340,7 @@ int check_sticky_error(moe_engine* eng, cudaStream_t st) {
     if (cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone) {
         CUDA_TRY(cudaDeviceSynchronize());
         *reinterpret_cast<volatile int32_t*>(eng->herr) = 0;
-        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
+        CUDA_TRY(cudaMemset(eng->bar, 0, bar_bytes(eng)));
     }
     return fail(MOE_ERR_DEVICE, std::string("an earlier launch on this engine failed on the device: error ") +
                                     std::to_string(v) + " (" + device_error_meaning(v) +
@@ -1389,6 +1398,8 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (const char* v = std::getenv("MOE_SK_MIN_CHUNKS")) eng->sk_min_chunks_per_cta = std::max(0, std::atoi(v));
     eng->max_smem = (int)prop.sharedMemPerBlockOptin;
     if (eng->cl_max_tokens < 0) eng->cl_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 1;  // where it is faster
+    if (const char* v = std::getenv("MOE_TP_MAX_TOKENS")) eng->tp_max_tokens = std::atoi(v);
+    if (eng->tp_max_tokens < 0) eng->tp_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 0;
     int rc = MOE_OK;
     rc = alloc_q_layout(eng);
     if (rc == MOE_OK) rc = ensure_workspace(eng, 64);
@@ -1556,6 +1567,71 @@ extern "C" int moe_engine_load_awq(moe_engine* eng, const void* w13_qw, const vo
     return MOE_OK;
 }
 
+// ============================================================ two-pass decode (AWQ)
+struct TpPlan {
+    TpParams p;
+    size_t smem1, smem2;
+};
+
+// Plan of the two-pass kernels for T tokens; false when they do not apply.
+bool plan_decode_tp(moe_engine* eng, int T, int K, TpPlan& pl) {
+    if (eng->cfg.quant_type != MOE_AWQ || T < 1 || T > eng->tp_max_tokens || T * K > kTpMaxPairs) return false;
+    if (!eng->agu || !eng->adn || !awq_recs_ok(eng)) return false;
+    const int H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
+    if (H % kAwqK || I % kAwqK) return false;
+    TpParams& p = pl.p;
+    std::memset(&p, 0, sizeof(p));
+    p.E = (int)eng->cfg.num_experts; p.e_off = (int)eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
+    p.emap = eng->emap; p.emap_n = eng->emap_n;
+    p.flags = eng->decode_flags;
+    p.ncol = std::min(T, kTpCols);
+    pl.smem1 = (size_t)2 * (H / kAwqK) * kAwqGuRec + (size_t)T * (H + 8) * 2 + (size_t)T * (H / kAwqK) * 4;
+    pl.smem2 = (size_t)(I / kAwqK) * kAwqDnRec + (size_t)p.ncol * (I + 8) * 2 + (size_t)p.ncol * (I / kAwqK) * 4;
+    const size_t lim = (size_t)eng->max_smem - 16384;  // static shared memory of the kernels (< 16 KB)
+    return pl.smem1 <= lim && pl.smem2 <= lim;
+}
+
+template <bool XBF>
+int launch_decode_tp(moe_engine* eng, TpPlan& pl, cudaStream_t st) {
+    static thread_local bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_set[dev]) {
+        // the largest dynamic share each kernel can have next to its static shared memory
+        cudaFuncAttributes fa{}, fb{};
+        CUDA_TRY(cudaFuncGetAttributes(&fa, tp_gate_up_kernel<XBF>));
+        CUDA_TRY(cudaFuncGetAttributes(&fb, tp_down_kernel<XBF>));
+        CUDA_TRY(cudaFuncSetAttribute(tp_gate_up_kernel<XBF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      eng->max_smem - (int)fa.sharedSizeBytes));
+        CUDA_TRY(cudaFuncSetAttribute(tp_down_kernel<XBF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      eng->max_smem - (int)fb.sharedSizeBytes));
+        // one shared-memory carveout for both, so that pass 2's CTAs can start on SMs that
+        // still run pass 1's (a different carveout waits for the SM to drain)
+        CUDA_TRY(cudaFuncSetAttribute(tp_gate_up_kernel<XBF>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        CUDA_TRY(cudaFuncSetAttribute(tp_down_kernel<XBF>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        if (dev < 64) attr_set[dev] = true;
+    }
+    const TpParams& p = pl.p;
+    cudaLaunchAttribute attr[1];
+    // programmatic dependent launch: each kernel waits (griddepcontrol.wait) for its stream
+    // predecessor before it reads that one's output
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(kTpWarpsA * 32);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = eng->pdl ? 1 : 0;
+    cfg.gridDim = dim3(p.I / 16, p.T * p.K);
+    cfg.dynamicSmemBytes = pl.smem1;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, tp_gate_up_kernel<XBF>, p));
+    cfg.gridDim = dim3(p.H / 32, p.T * p.K);
+    cfg.blockDim = dim3(kTpWarpsB * 32);
+    cfg.dynamicSmemBytes = pl.smem2;
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, tp_down_kernel<XBF>, p));
+    return MOE_OK;
+}
+
 extern "C" int moe_engine_reserve(moe_engine* eng, int64_t max_tokens, int64_t top_k) {
     if (int rc = check_engine(eng)) return rc;
     if (max_tokens < 0 || top_k <= 0) return fail(MOE_ERR_INVALID, "bad reserve size");
@@ -1639,7 +1715,34 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         }
         return MOE_OK;
     }
-    // decode sizes: the cluster kernel when it applies
+    // decode sizes: the two-pass kernels, else the cluster kernel, when they apply
+    if (!eng->p2p_active && T <= eng->tp_max_tokens) {
+        TpPlan tp;
+        if (plan_decode_tp(eng, (int)T, (int)K, tp)) {
+            if (int rc = ensure_clpart(eng, T * K)) return rc;   // part [T K][H]
+            if (int rc = ensure_workspace(eng, T * K)) return rc;  // h, counters, error word
+            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+            CUDA_TRY(cudaStreamIsCapturing(st, &cap));
+            const bool timed = cap == cudaStreamCaptureStatusNone;
+            if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
+            TpParams& p = tp.p;
+            p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+            p.x = x; p.y = y; p.ids = topk_ids; p.tw = topk_w;
+            p.gu = eng->agu; p.dn = eng->adn;
+            p.h = reinterpret_cast<uint16_t*>(eng->h_ws);
+            p.part = eng->clpart;
+            p.cnt = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(eng->bar) + 256);
+            p.err = eng->err;
+            p.dbg = eng->timeline_ctas >= (int)(std::max<int64_t>(H / 32, p.I / 16) * T * K) ? eng->timeline : nullptr;
+            const int rc = act_dtype == MOE_BF16 ? launch_decode_tp<true>(eng, tp, st) : launch_decode_tp<false>(eng, tp, st);
+            if (rc) return rc;
+            if (timed) {
+                CUDA_TRY(cudaEventRecord(eng->ev1, st));
+                eng->timed = true;
+            }
+            return MOE_OK;
+        }
+    }
     if (!eng->p2p_active && T <= eng->cl_max_tokens) {
         ClPlan cp;
         const int qt = eng->cfg.quant_type;
@@ -1811,7 +1914,7 @@ extern "C" int moe_engine_device_error(moe_engine* eng, int32_t* code) {
     *code = v;
     if (v != 0) {  // clear the error word and the barrier state
         *reinterpret_cast<volatile int32_t*>(eng->herr) = 0;
-        CUDA_TRY(cudaMemset(eng->bar, 0, 256));
+        CUDA_TRY(cudaMemset(eng->bar, 0, bar_bytes(eng)));
     }
     return MOE_OK;
 }
@@ -1919,9 +2022,12 @@ extern "C" int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64
     if (int rc = check_engine(eng)) return rc;
     DeviceGuard g(eng->cfg.device);
     if (enable && !eng->timeline) {
-        CUDA_TRY(cudaMalloc(&eng->timeline, (size_t)eng->num_sms * kStamps * sizeof(unsigned long long)));
-        CUDA_TRY(cudaMemset(eng->timeline, 0, (size_t)eng->num_sms * kStamps * sizeof(unsigned long long)));
-        eng->timeline_ctas = eng->num_sms;
+        // one row per CTA: the persistent kernels use num_sms rows, the two-pass kernels up to
+        // (row tiles x pieces) rows
+        const int rows = std::max(eng->num_sms, 1024);
+        CUDA_TRY(cudaMalloc(&eng->timeline, (size_t)rows * kStamps * sizeof(unsigned long long)));
+        CUDA_TRY(cudaMemset(eng->timeline, 0, (size_t)rows * kStamps * sizeof(unsigned long long)));
+        eng->timeline_ctas = rows;
     }
     if (!enable && eng->timeline) {
         CUDA_TRY(cudaDeviceSynchronize());

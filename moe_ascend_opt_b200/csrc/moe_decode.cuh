@@ -183,8 +183,10 @@ MOE_DEV RouteSmem carve_route(int32_t* base, int TK, int E) {
 // __match_any_sync, so positions inside an expert follow pair order exactly.
 MOE_DEV void route_warp(const int32_t* g_ids, int TK, int K, int E, int e_off, const int32_t* emap, int emap_n, RouteSmem r,
                         int lane) {
+#pragma unroll 1
     for (int e = lane; e < E; e += 32) r.cnt[e] = 0;
     __syncwarp();
+#pragma unroll 1
     for (int i0 = 0; i0 < TK; i0 += 32) {
         const int i = i0 + lane;
         int e = -1;
@@ -205,6 +207,7 @@ MOE_DEV void route_warp(const int32_t* g_ids, int TK, int K, int E, int e_off, c
     // contiguous experts [l*c, l*c + c); one warp scan of (actives << 16 | count).
     const int c = (E + 31) >> 5;
     int loc = 0;
+#pragma unroll 1
     for (int k = 0; k < c; ++k) {
         const int e = lane * c + k;
         const int n = e < E ? r.cnt[e] : 0;
@@ -217,6 +220,7 @@ MOE_DEV void route_warp(const int32_t* g_ids, int TK, int K, int E, int e_off, c
         if (lane >= o) incl += v;
     }
     int run = incl - loc;  // exclusive prefix of this lane's chunk
+#pragma unroll 1
     for (int k = 0; k < c; ++k) {
         const int e = lane * c + k;
         if (e >= E) break;
@@ -237,6 +241,7 @@ MOE_DEV void route_warp(const int32_t* g_ids, int TK, int K, int E, int e_off, c
         *r.nuniq = ucarry;
     }
     __syncwarp();
+#pragma unroll 1
     for (int i = lane; i < TK; i += 32) {
         const int e = r.ids[i];
         if (e >= 0) {
@@ -364,6 +369,7 @@ MOE_DEV void quant_x_quad(const uint8_t* x, int act_bf16, int nrows, int cols, i
                           int tid, int nthreads) {
     const int nblk = nrows * (cols >> 5), sub = tid & 3;
     const uint32_t qm = quad_mask(tid & 31);
+#pragma unroll 1
     for (int g = tid >> 2; g < nblk; g += nthreads >> 2) {  // the 4 threads of a quad share g
         float v[8];
         const uint4 r = __ldg(reinterpret_cast<const uint4*>(x + (size_t)g * 64) + sub);

@@ -127,13 +127,13 @@ MOE_DEV unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
 template <bool BF>
 MOE_DEV void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     if constexpr (BF)
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%0,%1,%2,%3};"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
     else
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%0,%1,%2,%3};"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -151,42 +151,64 @@ MOE_DEV float from16(uint16_t b) {
     else return __half2float(__ushort_as_half(b));
 }
 
-// One 16-row x 64-k AWQ tile (q at `q`, 32 B per row; scales `sc`, zeros `zp`, one per
-// row) against the B rows of up to 8 positions: brow = this lane's 16-bit row (position
-// lane/4) at the tile's first k, or nullptr; xs0 / xs1 = the sums of the B rows of
-// positions 2c / 2c+1 over the tile's k.  Adds the folded products to tot[4] = rows
-// (g, g+8) x positions (2c, 2c+1).
+// The A fragments of one 16-row x 64-k AWQ tile (q at `q`, 32 B per row) for the four
+// k16 steps of mma.sync m16n8k16: a[4 s + i] = register i of step s, each two 16-bit values
+// M + q exactly (bf16: M = 128, fp16: M = 1024).
 template <bool BF>
-MOE_DEV void awq_mma64(const uint8_t* q, const uint16_t* sc, const uint8_t* zp, const uint16_t* brow, float xs0,
-                       float xs1, int lane, float (&tot)[4]) {
+MOE_DEV void awq_frag64(const uint8_t* q, int lane, uint32_t (&a)[16]) {
     constexpr uint32_t kMagic = BF ? 0x43004300u : 0x64006400u;
-    constexpr float kM = BF ? 128.0f : 1024.0f;
     const int g = lane >> 2, c = lane & 3;
     const uint2 qa = *reinterpret_cast<const uint2*>(q + g * 32 + c * 8);
     const uint2 qb = *reinterpret_cast<const uint2*>(q + (g + 8) * 32 + c * 8);
     const uint32_t wa[2] = {qa.x, qa.y}, wb[2] = {qb.x, qb.y};
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const int j = s >> 1, sh = (s & 1) * 8;
-        uint32_t a[4];
-        a[0] = ((wa[j] >> sh) & 0x000F000Fu) | kMagic;        // row g,   k 2c, 2c+1
-        a[1] = ((wb[j] >> sh) & 0x000F000Fu) | kMagic;        // row g+8, k 2c, 2c+1
-        a[2] = ((wa[j] >> (sh + 4)) & 0x000F000Fu) | kMagic;  // row g,   k 2c+8, 2c+9
-        a[3] = ((wb[j] >> (sh + 4)) & 0x000F000Fu) | kMagic;  // row g+8, k 2c+8, 2c+9
+        a[4 * s + 0] = ((wa[j] >> sh) & 0x000F000Fu) | kMagic;        // row g,   k 2c, 2c+1
+        a[4 * s + 1] = ((wb[j] >> sh) & 0x000F000Fu) | kMagic;        // row g+8, k 2c, 2c+1
+        a[4 * s + 2] = ((wa[j] >> (sh + 4)) & 0x000F000Fu) | kMagic;  // row g,   k 2c+8, 2c+9
+        a[4 * s + 3] = ((wb[j] >> (sh + 4)) & 0x000F000Fu) | kMagic;  // row g+8, k 2c+8, 2c+9
+    }
+}
+
+// The tile's products from its fragments against the B rows of up to 8 positions: brow = this
+// lane's 16-bit row (position lane/4) at the tile's first k, or nullptr; xs0 / xs1 = the sums
+// of the B rows of positions 2c / 2c+1 over the tile's k; s0 / s1 and z0 / z1 = scale and zero
+// point of rows g and g+8.  Adds s (D - (M + z) sum_k x_k) to tot[4] = rows (g, g+8) x
+// positions (2c, 2c+1).
+template <bool BF>
+MOE_DEV void awq_mma64_frag(const uint32_t (&a)[16], float s0, float s1, float z0, float z1, const uint16_t* brow,
+                            float xs0, float xs1, int lane, float (&tot)[4]) {
+    constexpr float kM = BF ? 128.0f : 1024.0f;
+    const int c = lane & 3;
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
         uint32_t b0 = 0, b1 = 0;
         if (brow) {
             b0 = *reinterpret_cast<const uint32_t*>(brow + 16 * s + 2 * c);
             b1 = *reinterpret_cast<const uint32_t*>(brow + 16 * s + 2 * c + 8);
         }
-        mma16816<BF>(d, a, b0, b1);
+        const uint32_t as[4] = {a[4 * s], a[4 * s + 1], a[4 * s + 2], a[4 * s + 3]};
+        mma16816<BF>(d, as, b0, b1);
     }
-    const float s0 = __uint_as_float((uint32_t)sc[g] << 16), s1 = __uint_as_float((uint32_t)sc[g + 8] << 16);
-    const float m0 = kM + (float)zp[g], m1 = kM + (float)zp[g + 8];
+    const float m0 = kM + z0, m1 = kM + z1;
     tot[0] = fmaf(s0, fmaf(-m0, xs0, d[0]), tot[0]);
     tot[1] = fmaf(s0, fmaf(-m0, xs1, d[1]), tot[1]);
     tot[2] = fmaf(s1, fmaf(-m1, xs0, d[2]), tot[2]);
     tot[3] = fmaf(s1, fmaf(-m1, xs1, d[3]), tot[3]);
+}
+
+// One 16-row x 64-k AWQ tile (q at `q`, 32 B per row; scales `sc`, zeros `zp`, one per
+// row): awq_frag64 then awq_mma64_frag.
+template <bool BF>
+MOE_DEV void awq_mma64(const uint8_t* q, const uint16_t* sc, const uint8_t* zp, const uint16_t* brow, float xs0,
+                       float xs1, int lane, float (&tot)[4]) {
+    uint32_t a[16];
+    awq_frag64<BF>(q, lane, a);
+    const int g = lane >> 2;
+    awq_mma64_frag<BF>(a, __uint_as_float((uint32_t)sc[g] << 16), __uint_as_float((uint32_t)sc[g + 8] << 16),
+                       (float)zp[g], (float)zp[g + 8], brow, xs0, xs1, lane, tot);
 }
 
 // Contiguous per-warp ranges [floor(w N / W), floor((w+1) N / W)) of N items.
@@ -213,6 +235,7 @@ template <bool Q4>
 MOE_DEV void requant_smem(const float* h, int mc, int KR, int8_t* q, float* d, int32_t* s, int tid) {
     const int nblk = mc * (KR >> 5), sub = tid & 3;
     const uint32_t qm = quad_mask(tid & 31);
+    #pragma unroll 1
     for (int g = tid >> 2; g < nblk; g += kClThreads / 4) {
         float v[8];
         const float4 a = *reinterpret_cast<const float4*>(h + (size_t)g * 32 + sub * 8);
@@ -330,7 +353,7 @@ __device__ __forceinline__ void cl_top_up(const ClParams& p, const ClGeo& g, ClW
     }
 }
 
-template <int FMT, bool XBF>
+template <int FMT, bool XBF, int TF>
 __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClParams p) {
     constexpr bool Q4 = FMT == kQ4;
     constexpr bool AWQ = FMT == kAWQ;
@@ -338,7 +361,10 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     constexpr int SB = 32 * BB + 64;          // Q8/Q4 down row-slice record
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int TK = p.T * p.K, E = p.E, H = p.H, I = p.I, T = p.T;
+    // TF > 0: the token count fixed at compile time (the one-token decode variant is a smaller
+    // program); 0: p.T
+    const int T = TF > 0 ? TF : p.T;
+    const int TK = T * p.K, E = p.E, H = p.H, I = p.I;
     const int nb1 = H >> 5;
     const int cs = (int)cl_size(), rank = (int)cl_rank(), cid = (int)cl_id(), NC = (int)cl_count();
     const int RPC = H / cs;  // down rows of this CTA
@@ -352,9 +378,11 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     };
     auto flush_stamps = [&]() {
         if (dbg && tid == 0)
+            #pragma unroll 1
             for (int i = 0; i < kStamps; ++i) dbg[i] = s_st[i];
     };
     if (dbg && tid == 0)
+        #pragma unroll 1
         for (int i = 0; i < kStamps; ++i) s_st[i] = 0;
     stamp(0);
 
@@ -370,6 +398,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     // ---------------- routing, work units, token staging ----------------
     if (tid == 0) s_last = 0u;
     if (lane == 0)
+        #pragma unroll 1
         for (int s = 0; s < kClInFlight; ++s) mbar_init(&mybar[s], 1);
     // Programmatic dependent launch: the next kernel on the stream may be scheduled now (it
     // waits for this grid's completion before it reads anything); this grid waits here for
@@ -383,6 +412,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         // first piece
         const int U = *rt.nuniq, cu = (U + 31) >> 5;
         int loc = 0;
+        #pragma unroll 1
         for (int k = 0; k < cu; ++k) {
             const int u = lane * cu + k;
             if (u < U) loc += (rt.ucnt[u] + T - 1) / T;
@@ -396,15 +426,18 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         const int P = __shfl_sync(0xffffffffu, incl, 31);
         // Q minimises the busiest cluster's share ceil(P Q / NC) / Q, ties to the smaller Q
         int bq = 1, bnum = 0x7fffffff, bden = 1;
+        #pragma unroll 1
         for (int lq = 0; (1 << lq) <= kClMaxQ; ++lq) {
             if (!((p.qmask >> lq) & 1)) continue;
             const int q = 1 << lq, num = (P * q + NC - 1) / NC;  // share = num / q
             if ((int64_t)num * bden < (int64_t)bnum * q) { bq = q; bnum = num; bden = q; }
         }
         int w0 = (incl - loc) * bq;
+        #pragma unroll 1
         for (int k = 0; k < cu; ++k) {
             const int u = lane * cu + k;
             if (u >= U) break;
+            #pragma unroll 1
             for (int m0 = 0; m0 < rt.ucnt[u]; m0 += T)
                 for (int q = 0; q < bq; ++q) wl[w0++] = (u << 16) | (m0 << 4) | q;
         }
@@ -415,12 +448,26 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     } else {
         if constexpr (AWQ) {
             // tokens as 16-bit rows [T][H + 8] (padded against bank conflicts)
+            // and the per-64 sums of each row [T][H/64]: eight neighbouring lanes hold one
+            // 64-run (the stride and the trip count are multiples of 8, so a run is never split)
             uint16_t* xs = reinterpret_cast<uint16_t*>(smem + p.off_x);
+            float* xsum_w = reinterpret_cast<float*>(smem + p.off_x + (size_t)T * (H + 8) * 2);
             const uint16_t* xg = static_cast<const uint16_t*>(p.x);
+            #pragma unroll 1
             for (int i = tid; i < T * (H / 8); i += kClThreads - 32) {
                 const int t = i / (H / 8), k8 = i - t * (H / 8);
-                *reinterpret_cast<uint4*>(xs + (size_t)t * (H + 8) + 8 * k8) =
-                    __ldg(reinterpret_cast<const uint4*>(xg + (size_t)t * H) + k8);
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(xg + (size_t)t * H) + k8);
+                *reinterpret_cast<uint4*>(xs + (size_t)t * (H + 8) + 8 * k8) = v;
+                float sv = 0.f;
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    sv += from16<XBF>((uint16_t)(w4[j] & 0xffffu)) + from16<XBF>((uint16_t)(w4[j] >> 16));
+                const unsigned am = __activemask();
+                sv += __shfl_xor_sync(am, sv, 1);
+                sv += __shfl_xor_sync(am, sv, 2);
+                sv += __shfl_xor_sync(am, sv, 4);
+                if ((k8 & 7) == 0) xsum_w[t * NK1 + (k8 >> 3)] = sv;
             }
         } else {
             int8_t* xq = reinterpret_cast<int8_t*>(smem + p.off_x);
@@ -429,18 +476,13 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
             quant_x_quad<Q4>(static_cast<const uint8_t*>(p.x), p.act_bf16, T, H, xq, xd, xsm, tid, kClThreads - 32);
         }
     }
+    stamp(12);
     fence_barrier_init();
     __syncthreads();
+    stamp(13);
     float* xsum = nullptr;  // AWQ: per-64 sums of the token rows [T][H/64]
     if constexpr (AWQ) {
-        const uint16_t* xs = reinterpret_cast<const uint16_t*>(smem + p.off_x);
         xsum = reinterpret_cast<float*>(smem + p.off_x + (size_t)T * (H + 8) * 2);
-        for (int i = warp; i < T * NK1; i += kClWarps) {
-            const int t = i / NK1, kh = i - t * NK1;
-            const uint16_t* r = xs + (size_t)t * (H + 8) + kh * kAwqK;
-            const float sv = warp_sum64<XBF>(r, lane);
-            if (lane == 0) xsum[i] = sv;
-        }
     }
     stamp(1);
     const int NW = s_nwu, Q = s_q;
@@ -448,10 +490,12 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
 
     if (p.meta && cid == 0 && rank == 0) {  // the separate combine kernel reads Q and the scatter map
         if (tid == 0) p.meta[0] = Q;
+        #pragma unroll 1
         for (int i = tid; i < TK; i += kClThreads) p.meta[1 + i] = rt.smap[i];
     }
     if (NW == 0) {  // no routed pair on this engine: the output is zero (q8_gemm.cpp:328-333)
         if (cid == 0 && !p.meta)
+            #pragma unroll 1
             for (int idx = tid; idx < T * RPC; idx += kClThreads) {
                 const int t = idx / RPC, n = rank * RPC + idx % RPC;
                 const size_t o = (size_t)t * H + n;
@@ -482,6 +526,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
             W.g_lo = range_lo(warp, N1);
             W.g_n = range_lo(warp + 1, N1) - W.g_lo;
             int n1 = 0;  // runs of <= upi records inside each row tile
+            #pragma unroll 1
             for (int it = W.g_lo; it < W.g_lo + W.g_n;) {
                 const int rti = it / NK1, end = min(W.g_lo + W.g_n, (rti + 1) * NK1);
                 n1 += (end - it + p.upi - 1) / p.upi;
@@ -504,9 +549,11 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         W.head = 0;
     }
     __syncwarp();
+    stamp(14);
     const int n1 = W.n1, d_lo = W.d_lo, d_n = W.d_n, per_slice = W.per_slice;
     const int dpi = p.kpi;  // records / blocks per down item
     const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
+    stamp(15);
     if (lane == 0) cl_top_up<FMT>(p, geo, W, wl, rt.ue, myring, mybar, myoff, 0, pol);
     __syncwarp();
     stamp(6);
@@ -567,12 +614,14 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
                 }
                 tot[0] = tot[1] = tot[2] = tot[3] = 0.f;
             };
+            #pragma unroll 1
             for (int i = 0; i < n1; ++i) {
                 const uint8_t* slot = wait_item();
                 int first, cnt;
                 gu_item(i, first, cnt);
                 const int rti = first / NK1;
                 if (rti != cur) { flush(); cur = rti; }
+                #pragma unroll 1
                 for (int r = 0; r < cnt; ++r) {
                     const int kh = first + r - rti * NK1;
                     const uint8_t* rec = slot + (size_t)r * kAwqGuRec;
@@ -587,14 +636,17 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
             __syncthreads();
             // h[m][j] = SiLU(gate) * up over the CTA's units, slots summed in warp order
             uint16_t* hl16 = reinterpret_cast<uint16_t*>(hl);
+            #pragma unroll 1
             for (int idx = tid; idx < mc * UPC; idx += kClThreads) {
                 const int m = idx / UPC, j = idx - m * UPC;
                 const int ut = j >> 4, r = j & 15;
                 float gu2[2];
+                #pragma unroll 1
                 for (int half = 0; half < 2; ++half) {
                     const int rti = 2 * ut + half;
                     const int ns = item_owner(rti * NK1 + NK1 - 1, N1) - item_owner(rti * NK1, N1) + 1;
                     float acc = 0.f;
+                    #pragma unroll 1
                     for (int sl = 0; sl < ns; ++sl) acc += P1[((size_t)rti * nslot + sl) * 16 * cap + r * cap + m];
                     gu2[half] = acc;
                 }
@@ -608,10 +660,12 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
             const int32_t* xsm = reinterpret_cast<const int32_t*>(xd + (size_t)T * nb1);
             float* hlf = reinterpret_cast<float*>(hl);
             const int ub = 2 * (p.rs1 + p.ss1);
+            #pragma unroll 1
             for (int i = 0; i < n1; ++i) {
                 const uint8_t* slot = wait_item();
                 int first, cnt;
                 gu_item(i, first, cnt);
+                #pragma unroll 1
                 for (int uu = 0; uu < cnt; ++uu) {  // one unit at a time, all lanes over its blocks
                     const uint8_t* rec = slot + (size_t)uu * ub;
                     const uint8_t* qg = rec;
@@ -659,6 +713,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         if constexpr (AWQ) {
             const uint32_t* src = reinterpret_cast<const uint32_t*>(hl);  // pairs of 16-bit values
             const int np = UPC / 2;
+            #pragma unroll 1
             for (int idx = tid; idx < cs * mc * np; idx += kClThreads) {
                 const int qr = idx / (mc * np), rem = idx - qr * (mc * np);
                 const int m = rem / np, pr = rem - m * np;
@@ -668,6 +723,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         } else {
             const float4* src = reinterpret_cast<const float4*>(hl);
             const int nv = UPC / 4;
+            #pragma unroll 1
             for (int idx = tid; idx < cs * mc * nv; idx += kClThreads) {
                 const int qr = idx / (mc * nv), rem = idx - qr * (mc * nv);
                 const int m = rem / nv, v = rem - m * nv;
@@ -686,6 +742,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         if constexpr (AWQ) {
             const uint16_t* h16 = reinterpret_cast<const uint16_t*>(hb);
             float* hsum = reinterpret_cast<float*>(hqb);  // [cap][KH] per-64 sums of h (GU slots are free)
+            #pragma unroll 1
             for (int i = warp; i < mc * KH; i += kClWarps) {
                 const int m = i / KH, kh = i - m * KH;
                 const uint16_t* r = h16 + (size_t)m * (KR + 8) + kh * kAwqK;
@@ -696,11 +753,14 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
             const int g = lane >> 2, c = lane & 3;
             const uint16_t* hrow = g < mc ? h16 + (size_t)g * (KR + 8) : nullptr;
             const int c0 = min(2 * c, mc - 1), c1 = min(2 * c + 1, mc - 1);
+            #pragma unroll 1
             for (int sl = 0; sl < d_n; ++sl) {  // a 32-row block, its whole K-range in this warp
                 float tot[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                #pragma unroll 1
                 for (int pc = 0; pc < per_slice; ++pc) {
                     const uint8_t* slot = wait_item();
                     const int nn = min(dpi, KH - pc * dpi);
+                    #pragma unroll 1
                     for (int r = 0; r < nn; ++r) {
                         const int kh = pc * dpi + r;  // K-range local
                         const uint8_t* rec = slot + (size_t)r * kAwqDnRec;
@@ -737,16 +797,19 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
             int32_t* hs = reinterpret_cast<int32_t*>(hd + (size_t)cap * KB);
             requant_smem<Q4>(hf, mc, KR, hq, hd, hs, tid);
             __syncthreads();
+            #pragma unroll 1
             for (int sl = 0; sl < d_n; ++sl) {  // lane = row of the 32-row slice
                 float acc[8];
 #pragma unroll
                 for (int m = 0; m < 8; ++m) acc[m] = 0.f;
+                #pragma unroll 1
                 for (int pc = 0; pc < per_slice; ++pc) {
                     const uint8_t* slot = wait_item();
                     const int nn = min(dpi, KB - pc * dpi);
 #pragma unroll 1
                     for (int m = 0; m < mc; ++m) {  // one token at a time: small code
                         float am = 0.f;
+                        #pragma unroll 1
                         for (int r = 0; r < nn; ++r) {
                             const int b = pc * dpi + r;  // K-range local 32-block
                             const uint8_t* rec = slot + (size_t)r * SB;
@@ -770,6 +833,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
         }
         __syncthreads();
         // the routed pairs' partial rows of this CTA into `part` [(pos * Q + q)][H] (coalesced)
+        #pragma unroll 1
         for (int idx = tid; idx < mc * RPC; idx += kClThreads) {
             const int m = idx / RPC, r = idx - m * RPC;
             __stcg(p.part + ((size_t)(ps + m) * Q + q) * H + rank * RPC + r, outs[idx]);
@@ -778,6 +842,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     };
 
     // ---------------- work units ----------------
+    #pragma unroll 1
     for (int k = 0; k < n_my; ++k) {
         gate_up(k);
         if (k == 0) stamp(3);
@@ -794,6 +859,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
 
     // drain: a warp that stopped early still waits (bounded) for its copies in flight
     if (!ok && lane == 0)
+        #pragma unroll 1
         for (int i = consumed; i < W.nissued; ++i) mbar_wait(&mybar[i % kClInFlight], (uint32_t)(i / kClInFlight) & 1u);
 
     // ---------------- combine ----------------
@@ -822,13 +888,16 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
     // every load is coalesced): for each routed pair in k order, its Q K-range partials, all
     // loads of 4 pairs in flight together, summed in q order, weighted and accumulated in k order
     const int nl = __popc(last);
+    #pragma unroll 1
     for (int idx = tid; idx < nl * T * RB; idx += kClThreads) {
         const int bi = idx / (T * RB), rem = idx - bi * (T * RB);
         int b = 0;
+        #pragma unroll 1
         for (int seen = -1; ; ++b)
             if ((last >> b) & 1u) { if (++seen == bi) break; }
         const int t = rem / RB, n = (blk0 + b) * RB + rem % RB;
         float acc = 0.f;
+        #pragma unroll 1
         for (int k0 = 0; k0 < p.K; k0 += 4) {
             int pos[4];
             float v[4];
@@ -837,6 +906,7 @@ __global__ void __launch_bounds__(kClThreads, 1) moe_decode_cl_kernel(const ClPa
                 pos[j] = k0 + j < p.K ? rt.smap[t * p.K + k0 + j] : -1;
                 v[j] = 0.f;
             }
+            #pragma unroll 1
             for (int q0 = 0; q0 < Q; q0 += 4) {
                 float a[4][4];
 #pragma unroll
@@ -876,6 +946,7 @@ __global__ void __launch_bounds__(256) cl_combine_kernel(const float* part, cons
     const int Q = __ldcg(meta);
     const int32_t* smap = meta + 1;
     float acc = 0.f;
+    #pragma unroll 1
     for (int k0 = 0; k0 < K; k0 += 4) {
         int pos[4];
         float v[4];
@@ -884,6 +955,7 @@ __global__ void __launch_bounds__(256) cl_combine_kernel(const float* part, cons
             pos[j] = k0 + j < K ? __ldcg(smap + t * K + k0 + j) : -1;
             v[j] = 0.f;
         }
+        #pragma unroll 1
         for (int q0 = 0; q0 < Q; q0 += 4) {
             float a[4][4];
 #pragma unroll

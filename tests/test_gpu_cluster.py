@@ -24,18 +24,20 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def make_engine(qt, E, H, I, seed, legacy=False, G=128, expert_offset=0):
+def make_engine(qt, E, H, I, seed, legacy=False, G=128, expert_offset=0, two_pass=False):
     """Engine with Q weights (or AWQ) that takes the cluster kernel for up to 8 tokens, or
-    (legacy=True) never."""
-    old = os.environ.get("MOE_CL_MAX_TOKENS")
-    os.environ["MOE_CL_MAX_TOKENS"] = "0" if legacy else "8"
+    (legacy=True) never; two_pass=True: the two-pass kernels (AWQ) for up to 8 tokens."""
+    env = {"MOE_CL_MAX_TOKENS": "0" if legacy else "8", "MOE_TP_MAX_TOKENS": "8" if two_pass else "0"}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
     try:
         eng = capi.Engine(E, H, I, qt, group_size=G, expert_offset=expert_offset)
     finally:
-        if old is None:
-            del os.environ["MOE_CL_MAX_TOKENS"]
-        else:
-            os.environ["MOE_CL_MAX_TOKENS"] = old
+        for k, v in old.items():
+            if v is None:
+                del os.environ[k]
+            else:
+                os.environ[k] = v
     if qt == capi.AWQ:
         wts = awq_weights(E, H, I, G, seed)
         eng.load_awq(*[torch.from_numpy(a) for a in wts])
