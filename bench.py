@@ -50,6 +50,27 @@ def tflops_peaks():
         return 1400.0
 
 
+def path_kernels(quant, T, K, E, peer_combine=False):
+    """(kernel(s) of the layer's path, launches per layer step) under the engine's default
+    dispatch: AWQ up to 8 tokens the two-pass kernels, up to 24 the grid-barrier decode kernel,
+    beyond that the tcgen05 grouped GEMMs; Q8_0 / Q4_0 up to 4 tokens the two-pass kernels, up to
+    8 the split-K decode kernel, beyond that the grouped GEMMs (route, quantise, two GEMMs,
+    combine)."""
+    if peer_combine:
+        return "moe_decode_kernel (peer combine)", 1
+    if quant == "awq":
+        if T <= 8:
+            return "tp_gate_up_kernel + tp_down_kernel", 2
+        if T <= 24:
+            return "moe_decode_kernel", 1
+        return "grouped_gemm_tc_kernel", 7
+    if T <= 4:
+        return "tp_gate_up_q_kernel + tp_down_q_kernel", 2
+    if T <= 8:
+        return "moe_decode_sk_kernel", 1
+    return ("grouped_gemm_wm_kernel" if T * K <= 24 * E else "grouped_gemm_kernel"), 7
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -504,7 +525,8 @@ def run_ours(args):
 
     out = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "us_per_layer": round(ms_step * 1e3, 3),
-           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "bf16" if args.quant == "awq" else "int8",
            "data": "synthetic",
            "config": {"workload": f"{qname} fused MoE layer H{H} I{I} E{E} top{K} T={T}"
                                   + (" (BASELINE configs[1])" if default_wl else f", {args.routing} routing"),
@@ -519,7 +541,7 @@ def run_ours(args):
                       "launch": (f"cuda_graph ({ncycle} layer steps per graph replay)" if cycle_graph is not None
                                  else "eager"),
                       "avg_active_experts": round(avg_bytes / bpe, 2)},
-           "gpu_launches": args.steps * (1 if T <= 8 or args.quant == "awq" else 7),
+           "gpu_launches": args.steps * path_kernels(args.quant, T, K, E, world > 1 and fused)[1],
            "clocks": clocks}
     if dev_errors:
         out["device_errors"] = dev_errors
@@ -528,9 +550,7 @@ def run_ours(args):
                            "frac": round(value / peak, 4), "peak_source": peak_kind,
                            "traffic": None,
                            "algorithmic_bytes_per_launch": round(avg_bytes),
-                           "kernel": ("moe_decode_kernel" if T == 1 or args.quant == "awq" else
-                                      "moe_decode_sk_kernel" if T <= 8 else
-                                      "grouped_gemm_wm_kernel" if T * K <= 24 * E else "grouped_gemm_kernel")}
+                           "kernel": path_kernels(args.quant, T, K, E, world > 1 and fused)[0]}
     # end-to-end through the public op with host buffers and copies in the timed region
     if rank == 0 or world > 1:
         # one pinned host buffer per step holding hidden | topk_ids | topk_w (16-byte aligned
@@ -758,7 +778,8 @@ def extra_block(quant, shape, routing, T, steps, dev, peak, nsets=16):
            "us_per_layer": round(ms * 1e3, 3), "value": round(val, 2), "unit": "GB/s", "steps": n,
            "avg_active_experts": round(avg_b / bpe, 2),
            "roofline": {"bound": "hbm", "achieved": round(val, 2), "peak": peak, "unit": "GB/s",
-                        "frac": round(val / peak, 4), "algorithmic_bytes_per_launch": round(avg_b)},
+                        "frac": round(val / peak, 4), "algorithmic_bytes_per_launch": round(avg_b),
+                        "kernel": path_kernels(quant, T, K, E_)[0]},
            "launch": f"cuda_graph ({ncyc} layer steps per replay, {nsets} weight sets)"}
     if errs:
         out["device_errors"] = errs

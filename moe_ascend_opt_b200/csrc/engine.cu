@@ -1399,7 +1399,7 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     eng->max_smem = (int)prop.sharedMemPerBlockOptin;
     if (eng->cl_max_tokens < 0) eng->cl_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 1;  // where it is faster
     if (const char* v = std::getenv("MOE_TP_MAX_TOKENS")) eng->tp_max_tokens = std::atoi(v);
-    if (eng->tp_max_tokens < 0) eng->tp_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 0;
+    if (eng->tp_max_tokens < 0) eng->tp_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 4;  // where it is faster
     int rc = MOE_OK;
     rc = alloc_q_layout(eng);
     if (rc == MOE_OK) rc = ensure_workspace(eng, 64);
@@ -1567,7 +1567,7 @@ extern "C" int moe_engine_load_awq(moe_engine* eng, const void* w13_qw, const vo
     return MOE_OK;
 }
 
-// ============================================================ two-pass decode (AWQ)
+// ============================================================ two-pass decode
 struct TpPlan {
     TpParams p;
     size_t smem1, smem2;
@@ -1575,43 +1575,68 @@ struct TpPlan {
 
 // Plan of the two-pass kernels for T tokens; false when they do not apply.
 bool plan_decode_tp(moe_engine* eng, int T, int K, TpPlan& pl) {
-    if (eng->cfg.quant_type != MOE_AWQ || T < 1 || T > eng->tp_max_tokens || T * K > kTpMaxPairs) return false;
-    if (!eng->agu || !eng->adn || !awq_recs_ok(eng)) return false;
+    const int qt = eng->cfg.quant_type;
+    if (T < 1 || T > eng->tp_max_tokens || T * K > kTpMaxPairs || !eng->adn) return false;
     const int H = (int)eng->cfg.hidden_size, I = (int)eng->cfg.intermediate_size;
-    if (H % kAwqK || I % kAwqK) return false;
+    const bool awq = qt == MOE_AWQ;
+    if (awq && (!eng->agu || !awq_recs_ok(eng) || H % kAwqK || I % kAwqK)) return false;
+    if (!awq && (H % 64 || I % 32)) return false;
     TpParams& p = pl.p;
     std::memset(&p, 0, sizeof(p));
     p.E = (int)eng->cfg.num_experts; p.e_off = (int)eng->cfg.expert_offset; p.H = H; p.I = I; p.T = T; p.K = K;
     p.emap = eng->emap; p.emap_n = eng->emap_n;
     p.flags = eng->decode_flags;
+    p.rs1 = eng->rs1; p.ss1 = eng->ss1;
+    p.scale_bf16 = eng->scale_bf16;
     p.ncol = std::min(T, kTpCols);
-    pl.smem1 = (size_t)2 * (H / kAwqK) * kAwqGuRec + (size_t)T * (H + 8) * 2 + (size_t)T * (H / kAwqK) * 4;
-    pl.smem2 = (size_t)(I / kAwqK) * kAwqDnRec + (size_t)p.ncol * (I + 8) * 2 + (size_t)p.ncol * (I / kAwqK) * 4;
+    if (awq) {
+        pl.smem1 = (size_t)2 * (H / kAwqK) * kAwqGuRec + (size_t)T * (H + 8) * 2 + (size_t)T * (H / kAwqK) * 4;
+        pl.smem2 = (size_t)(I / kAwqK) * kAwqDnRec + (size_t)p.ncol * (I + 8) * 2 + (size_t)p.ncol * (I / kAwqK) * 4;
+    } else {
+        const int64_t SB = 32 * (qt == MOE_Q4_0 ? 16 : 32) + 64;
+        pl.smem1 = (size_t)kTpUnitsQ * eng->unit_bytes() + (size_t)T * H + (size_t)T * (H / 32) * 8;
+        pl.smem2 = (size_t)(I / 32) * SB + (size_t)p.ncol * I + (size_t)p.ncol * (I / 32) * 8;
+    }
     const size_t lim = (size_t)eng->max_smem - 16384;  // static shared memory of the kernels (< 16 KB)
     return pl.smem1 <= lim && pl.smem2 <= lim;
 }
 
-template <bool XBF>
-int launch_decode_tp(moe_engine* eng, TpPlan& pl, cudaStream_t st) {
-    static thread_local bool attr_set[64] = {};
+// Largest dynamic shared memory next to the kernel's static share, and the full carveout, so
+// that pass 2's CTAs can start on SMs that still run pass 1's (a different carveout waits for
+// the SM to drain).  Once per kernel and device.
+int tp_kernel_attrs(const void* fn, int max_smem) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, int>> done;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !attr_set[dev]) {
-        // the largest dynamic share each kernel can have next to its static shared memory
-        cudaFuncAttributes fa{}, fb{};
-        CUDA_TRY(cudaFuncGetAttributes(&fa, tp_gate_up_kernel<XBF>));
-        CUDA_TRY(cudaFuncGetAttributes(&fb, tp_down_kernel<XBF>));
-        CUDA_TRY(cudaFuncSetAttribute(tp_gate_up_kernel<XBF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      eng->max_smem - (int)fa.sharedSizeBytes));
-        CUDA_TRY(cudaFuncSetAttribute(tp_down_kernel<XBF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      eng->max_smem - (int)fb.sharedSizeBytes));
-        // one shared-memory carveout for both, so that pass 2's CTAs can start on SMs that
-        // still run pass 1's (a different carveout waits for the SM to drain)
-        CUDA_TRY(cudaFuncSetAttribute(tp_gate_up_kernel<XBF>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        CUDA_TRY(cudaFuncSetAttribute(tp_down_kernel<XBF>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        if (dev < 64) attr_set[dev] = true;
-    }
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& d : done)
+        if (d.first == fn && d.second == dev) return MOE_OK;
+    cudaFuncAttributes fa{};
+    CUDA_TRY(cudaFuncGetAttributes(&fa, fn));
+    CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem - (int)fa.sharedSizeBytes));
+    CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    done.emplace_back(fn, dev);
+    return MOE_OK;
+}
+
+int launch_decode_tp(moe_engine* eng, TpPlan& pl, bool act_bf16, cudaStream_t st) {
     const TpParams& p = pl.p;
+    const int qt = eng->cfg.quant_type;
+    void (*k1)(TpParams);
+    void (*k2)(TpParams);
+    dim3 g1;
+    if (qt == MOE_AWQ) {
+        k1 = act_bf16 ? tp_gate_up_kernel<true> : tp_gate_up_kernel<false>;
+        k2 = act_bf16 ? tp_down_kernel<true> : tp_down_kernel<false>;
+        g1 = dim3(p.I / 16, p.T * p.K);
+    } else {
+        k1 = qt == MOE_Q4_0 ? tp_gate_up_q_kernel<true> : tp_gate_up_q_kernel<false>;
+        k2 = qt == MOE_Q4_0 ? tp_down_q_kernel<true> : tp_down_q_kernel<false>;
+        g1 = dim3((p.I + kTpUnitsQ - 1) / kTpUnitsQ, p.T * p.K);
+    }
+    if (int rc = tp_kernel_attrs(reinterpret_cast<const void*>(k1), eng->max_smem)) return rc;
+    if (int rc = tp_kernel_attrs(reinterpret_cast<const void*>(k2), eng->max_smem)) return rc;
     cudaLaunchAttribute attr[1];
     // programmatic dependent launch: each kernel waits (griddepcontrol.wait) for its stream
     // predecessor before it reads that one's output
@@ -1622,13 +1647,13 @@ int launch_decode_tp(moe_engine* eng, TpPlan& pl, cudaStream_t st) {
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = eng->pdl ? 1 : 0;
-    cfg.gridDim = dim3(p.I / 16, p.T * p.K);
+    cfg.gridDim = g1;
     cfg.dynamicSmemBytes = pl.smem1;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, tp_gate_up_kernel<XBF>, p));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, k1, p));
     cfg.gridDim = dim3(p.H / 32, p.T * p.K);
     cfg.blockDim = dim3(kTpWarpsB * 32);
     cfg.dynamicSmemBytes = pl.smem2;
-    CUDA_TRY(cudaLaunchKernelEx(&cfg, tp_down_kernel<XBF>, p));
+    CUDA_TRY(cudaLaunchKernelEx(&cfg, k2, p));
     return MOE_OK;
 }
 
@@ -1727,14 +1752,16 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
             if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
             TpParams& p = tp.p;
             p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+            p.act_bf16 = act_dtype == MOE_BF16;
             p.x = x; p.y = y; p.ids = topk_ids; p.tw = topk_w;
-            p.gu = eng->agu; p.dn = eng->adn;
-            p.h = reinterpret_cast<uint16_t*>(eng->h_ws);
+            p.gu = eng->cfg.quant_type == MOE_AWQ ? eng->agu : eng->gu;
+            p.dn = eng->adn;
+            p.h = eng->h_ws;
             p.part = eng->clpart;
             p.cnt = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(eng->bar) + 256);
             p.err = eng->err;
             p.dbg = eng->timeline_ctas >= (int)(std::max<int64_t>(H / 32, p.I / 16) * T * K) ? eng->timeline : nullptr;
-            const int rc = act_dtype == MOE_BF16 ? launch_decode_tp<true>(eng, tp, st) : launch_decode_tp<false>(eng, tp, st);
+            const int rc = launch_decode_tp(eng, tp, act_dtype == MOE_BF16, st);
             if (rc) return rc;
             if (timed) {
                 CUDA_TRY(cudaEventRecord(eng->ev1, st));

@@ -42,8 +42,10 @@ constexpr int kTpMaxPairs = 64;  // T * K of one launch
 constexpr int kTpCols = 8;       // pairs per piece (mma n)
 
 struct TpParams {
-    const uint8_t* gu;  // AWQ gate_up records
-    const uint8_t* dn;  // AWQ down records
+    const uint8_t* gu;  // AWQ gate_up records; Q8_0 / Q4_0 unit records [E][I] (gate row, up row, scales)
+    const uint8_t* dn;  // AWQ down records; Q8_0 / Q4_0 down row-slice records [E][H/32][I/32]
+    int32_t rs1, ss1;   // Q8_0 / Q4_0: quant and scale bytes of one row of a unit record
+    int32_t scale_bf16, act_bf16;
     int32_t E, e_off, H, I, T, K;
     const int32_t* emap;  // global -> local expert map (expert parallel) or null
     int32_t emap_n;
@@ -51,7 +53,7 @@ struct TpParams {
     void* y;                // output [T][H] (out_kind: 0 fp16, 1 bf16, 2 fp32)
     const int32_t* ids;     // [T][K] global expert ids
     const float* tw;        // [T][K] routing weights
-    uint16_t* h;            // [T K][I] activation-type h between the passes
+    void* h;                // h between the passes [T K][I]: AWQ activation type, Q8_0 / Q4_0 fp32
     float* part;            // [T K][H] weighted fp32 down rows
     unsigned int* cnt;      // [H/32] arrival counters, zero between launches
     int32_t* err;           // sticky device error word (mapped host memory)
@@ -284,7 +286,7 @@ __global__ void __launch_bounds__(kTpWarpsA * 32) tp_gate_up_kernel(const TpPara
             }
             const float hv = silu_mul(ga, ua);
             if (!XBF && !(fabsf(hv) <= 65504.f)) set_err(p.err, kErrRange);
-            p.h[(size_t)rt.pc[slot][n] * I + tile * 16 + r] = to16<XBF>(hv);
+            static_cast<uint16_t*>(p.h)[(size_t)rt.pc[slot][n] * I + tile * 16 + r] = to16<XBF>(hv);
         }
     }
     TP_STAMP(7);
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_kernel(const TpParams 
     #pragma unroll 1
     for (int i = tid; i < nc * (I / 8); i += kThreads) {
         const int n = i / (I / 8), k8 = i - n * (I / 8);
-        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.h + (size_t)rt.pc[slot][n] * I) + k8);
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.h) + (size_t)rt.pc[slot][n] * I) + k8);
         *reinterpret_cast<uint4*>(hs + (size_t)n * (I + 8) + 8 * k8) = v;
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
         float sv = 0.f;
@@ -434,6 +436,240 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_kernel(const TpParams 
         else reinterpret_cast<__half*>(p.y)[o] = __float2half_rn(acc);
     }
     TP_STAMP(18);
+}
+
+// ------------------------------------------------------------------ Q8_0 / Q4_0
+// The same two passes on the reference's 32-block formats: exact per-32-block integer dots
+// (dp4a) folded with the fp32 scales as gemm_kernels.cpp:66-186 does; the token rows
+// quantised to Q8_0 (gemm_kernels.cpp:25-58) by every pass-1 CTA, h kept in fp32 between the
+// passes and requantised by every pass-2 CTA for its piece (gemm_kernels.cpp:394-425).
+constexpr int kTpUnitsQ = 16;  // pass 1 (Q8/Q4): gate_up units per CTA, two per warp
+constexpr int kTpCopiesQ = 4;  // its bulk copies
+
+// The row block's combine by the CTA that completes its arrival count (see the file header).
+MOE_DEV void tp_arrive_combine(const TpParams& p, const TpRoute& rt, int rb, int tid, int nthreads,
+                               unsigned int* s_last) {
+    __syncthreads();
+    if (tid == 0) {  // release: the CTA's rows of `part`, ordered before by the barrier
+        unsigned int old;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.cnt + rb) : "memory");
+        *s_last = old == (unsigned int)(rt.P - 1);
+        if (*s_last) p.cnt[rb] = 0u;
+    }
+    __syncthreads();
+    if (!*s_last) return;
+    const int H = p.H, K = p.K;
+    #pragma unroll 1
+    for (int i = tid; i < p.T * 32; i += nthreads) {
+        const int t = i >> 5, row = rb * 32 + (i & 31);
+        float acc = 0.f;
+        #pragma unroll 1
+        for (int k0 = 0; k0 < K; k0 += 8) {
+            float v8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int j = t * K + k0 + k;
+                v8[k] = (k0 + k < K && rt.le[j] >= 0) ? __ldcg(p.part + (size_t)j * H + row) : 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc += v8[k];
+        }
+        const size_t o = (size_t)t * H + row;
+        if (p.out_kind == 2) reinterpret_cast<float*>(p.y)[o] = acc;
+        else if (p.out_kind == 1) reinterpret_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(acc);
+        else reinterpret_cast<__half*>(p.y)[o] = __float2half_rn(acc);
+    }
+}
+
+// Pass 1 (Q8/Q4): gate_up + SiLU * up of kTpUnitsQ units of one piece -> fp32 h.
+template <bool Q4>
+__global__ void __launch_bounds__(kTpWarpsA * 32) tp_gate_up_q_kernel(const TpParams p) {
+    constexpr int kThreads = kTpWarpsA * 32;
+    constexpr int BB = Q4 ? 16 : 32;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ TpRoute rt;
+    __shared__ __align__(8) uint64_t bars[kTpCopiesQ];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int H = p.H, I = p.I, nb1 = H >> 5;
+    const int ub = 2 * (p.rs1 + p.ss1);
+    const int tile = blockIdx.x, slot = blockIdx.y;
+    TP_STAMP(0);
+    if (tid < kTpCopiesQ) mbar_init(&bars[tid], 1);
+    fence_barrier_init();
+    tp_dep_wait(warp);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    TP_STAMP(1);
+    // warp 0 routes while the others quantise the T token rows (Q8_0, a quad per 32-block)
+    int8_t* xq = reinterpret_cast<int8_t*>(smem + (size_t)kTpUnitsQ * ub);
+    float* xd = reinterpret_cast<float*>(xq + (size_t)p.T * H);
+    int32_t* xsm = reinterpret_cast<int32_t*>(xd + (size_t)p.T * nb1);
+    if (warp == 0) tp_route(p, rt, lane);
+    else quant_x_quad<Q4>(static_cast<const uint8_t*>(p.x), p.act_bf16, p.T, H, xq, xd, xsm, tid - 32, kThreads - 32);
+    __syncthreads();
+    TP_STAMP(2);
+    if (slot >= rt.P) return;
+    const int e = rt.pe[slot], nc = rt.pn[slot];
+    const int u0 = tile * kTpUnitsQ, nu = min(kTpUnitsQ, I - u0);
+    if (lane == 0 && warp < kTpCopiesQ) {
+        const int a = warp * nu / kTpCopiesQ, n = (warp + 1) * nu / kTpCopiesQ - a;
+        const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
+        if (n > 0)
+            issue_copy(smem + (size_t)a * ub, p.gu + ((size_t)e * I + u0 + a) * ub, (uint32_t)n * ub, &bars[warp], pol);
+        else
+            mbar_arrive(&bars[warp]);
+    }
+    TP_STAMP(3);
+    const bool sbf = p.scale_bf16 != 0;
+    #pragma unroll 1
+    for (int uu = warp * kTpUnitsQ / kTpWarpsA; uu < (warp + 1) * kTpUnitsQ / kTpWarpsA; ++uu) {
+        if (uu >= nu) break;
+        tp_wait(p, &bars[uu * kTpCopiesQ / nu]);
+        const uint8_t* rec = smem + (size_t)uu * ub;
+        const uint8_t* qg = rec;
+        const uint8_t* qu = rec + p.rs1;
+        const uint16_t* sgate = reinterpret_cast<const uint16_t*>(rec + 2 * p.rs1);
+        const uint16_t* sup = reinterpret_cast<const uint16_t*>(rec + 2 * p.rs1 + p.ss1);
+        #pragma unroll 1
+        for (int m = 0; m < nc; ++m) {  // one token at a time: small code, weights from smem
+            const int t = rt.pc[slot][m] / p.K;
+            const int8_t* xt = xq + (size_t)t * H;
+            const float* xdt = xd + (size_t)t * nb1;
+            const int32_t* xst = xsm + (size_t)t * nb1;
+            float ag = 0.f, au = 0.f;
+#pragma unroll 2
+            for (int b = lane; b < nb1; b += 32) {
+                const uint4* wg = reinterpret_cast<const uint4*>(qg + (size_t)b * BB);
+                const uint4* wu4 = reinterpret_cast<const uint4*>(qu + (size_t)b * BB);
+                const uint4* a = reinterpret_cast<const uint4*>(xt + b * 32);
+                const float ad = xdt[b];
+                const int as = Q4 ? xst[b] : 0;
+                ag += ((float)block_dot<Q4>(wg, a, as) * scale_to_f32(sgate[b], sbf)) * ad;
+                au += ((float)block_dot<Q4>(wu4, a, as) * scale_to_f32(sup[b], sbf)) * ad;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                ag += __shfl_xor_sync(0xffffffffu, ag, o);
+                au += __shfl_xor_sync(0xffffffffu, au, o);
+            }
+            if (lane == 0) static_cast<float*>(p.h)[(size_t)rt.pc[slot][m] * I + u0 + uu] = silu_mul(ag, au);
+        }
+    }
+    TP_STAMP(7);
+}
+
+// Pass 2 (Q8/Q4): down rows of one 32-row block of one piece (lane = row of the block's
+// row-slice records), weighted into `part`, and the row block's combine.
+template <bool Q4>
+__global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_q_kernel(const TpParams p) {
+    constexpr int kThreads = kTpWarpsB * 32;
+    constexpr int BB = Q4 ? 16 : 32;
+    constexpr int SB = 32 * BB + 64;  // row-slice record: 32 rows x one 32-column block, 32 scales
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ TpRoute rt;
+    __shared__ __align__(8) uint64_t bars[kTpWarpsB];
+    __shared__ float red[kTpWarpsB][32][kTpCols];
+    __shared__ unsigned int s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int H = p.H, I = p.I, KB = I >> 5, T = p.T;
+    const int rb = blockIdx.x, slot = blockIdx.y;
+    TP_STAMP(10);
+    if (tid < kTpWarpsB) mbar_init(&bars[tid], 1);
+    fence_barrier_init();
+    if (warp == 0) tp_route(p, rt, lane);
+    __syncthreads();
+    TP_STAMP(11);
+    const int P = rt.P;
+    if (P == 0) {  // no routed pair on this engine: the output is zero (q8_gemm.cpp:328-333)
+        tp_dep_wait(warp);
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        if (slot == 0)
+            #pragma unroll 1
+            for (int i = tid; i < T * 32; i += kThreads) {
+                const size_t o = (size_t)(i >> 5) * H + rb * 32 + (i & 31);
+                if (p.out_kind == 2) reinterpret_cast<float*>(p.y)[o] = 0.f;
+                else if (p.out_kind == 1) reinterpret_cast<__nv_bfloat16*>(p.y)[o] = __float2bfloat16_rn(0.f);
+                else reinterpret_cast<__half*>(p.y)[o] = __float2half_rn(0.f);
+            }
+        return;
+    }
+    if (slot >= P) {
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        return;
+    }
+    const int e = rt.pe[slot], nc = rt.pn[slot];
+    const int b0 = warp * KB / kTpWarpsB, nbw = (warp + 1) * KB / kTpWarpsB - b0;
+    uint8_t* wd = smem + (size_t)b0 * SB;
+    if (lane == 0 && nbw > 0) {
+        const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
+        issue_copy(wd, p.dn + (((size_t)e * (H / 32) + rb) * KB + b0) * SB, (uint32_t)nbw * SB, &bars[warp], pol);
+    }
+    TP_STAMP(12);
+    if (nbw > 0) tp_wait(p, &bars[warp]);  // the records arrive while pass 1 still runs
+    TP_STAMP(15);
+    tp_dep_wait(warp);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    TP_STAMP(13);
+    // the piece's h rows requantised to Q8_0 [nc][I] | d [nc][KB] | sums [nc][KB], a quad per block
+    int8_t* hq = reinterpret_cast<int8_t*>(smem + (size_t)KB * SB);
+    float* hd = reinterpret_cast<float*>(hq + (size_t)p.ncol * I);
+    int32_t* hs = reinterpret_cast<int32_t*>(hd + (size_t)p.ncol * KB);
+    {
+        const int sub = tid & 3;
+        const uint32_t qm = quad_mask(lane);
+        #pragma unroll 1
+        for (int g = tid >> 2; g < nc * KB; g += kThreads / 4) {
+            const int m = g / KB, b = g - m * KB;
+            float v[8];
+            load8(static_cast<const float*>(p.h) + (size_t)rt.pc[slot][m] * I + b * 32 + sub * 8, v);
+            float dd;
+            int sum;
+            uint2 o;
+            quad_quant<Q4>(v, qm, dd, sum, o);
+            *reinterpret_cast<uint2*>(hq + (size_t)g * 32 + sub * 8) = o;
+            if (sub == 0) {
+                hd[g] = dd;
+                if (Q4) hs[g] = sum;
+            }
+        }
+    }
+    __syncthreads();
+    TP_STAMP(14);
+    const bool sbf = p.scale_bf16 != 0;
+    float acc[kTpCols];
+#pragma unroll
+    for (int m = 0; m < kTpCols; ++m) acc[m] = 0.f;
+    #pragma unroll 1
+    for (int r = 0; r < nbw; ++r) {
+        const int b = b0 + r;
+        const uint8_t* rec = wd + (size_t)r * SB;
+        const uint4* w = reinterpret_cast<const uint4*>(rec + lane * BB);
+        const float dw = scale_to_f32(reinterpret_cast<const uint16_t*>(rec + 32 * BB)[lane], sbf);
+#pragma unroll
+        for (int m = 0; m < kTpCols; ++m) {
+            if (m >= nc) break;
+            const uint4* a = reinterpret_cast<const uint4*>(hq + (size_t)m * I + b * 32);
+            const int is = block_dot<Q4>(w, a, Q4 ? hs[m * KB + b] : 0);
+            acc[m] += ((float)is * dw) * hd[m * KB + b];
+        }
+    }
+    TP_STAMP(16);
+#pragma unroll
+    for (int m = 0; m < kTpCols; ++m) red[warp][lane][m] = acc[m];
+    __syncthreads();
+    {
+        const int r = tid & 31;
+#pragma unroll
+        for (int n = tid >> 5; n < kTpCols; n += kTpWarpsB) {
+            if (n >= nc) continue;
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kTpWarpsB; ++w) v += red[w][r][n];
+            const int j = rt.pc[slot][n];
+            p.part[(size_t)j * H + rb * 32 + r] = __ldg(p.tw + j) * v;
+        }
+    }
+    tp_arrive_combine(p, rt, rb, tid, kThreads, &s_last);
+    TP_STAMP(17);
 }
 
 }  // namespace moe

@@ -1,10 +1,10 @@
-"""The two-pass AWQ decode kernels (tp_gate_up_kernel + tp_down_kernel: one CTA per row tile and
-piece, weights bulk-copied at CTA start, h between the passes in global memory, last-arriver
-combine per 32-row block) against the C oracle, the cluster kernel and the grid-barrier kernel,
-through the C ABI.  Covers T = 1..8, bf16 and fp16 activations, fp32 output, invalid ids,
-duplicate ids inside a token (more pieces than experts), calls with no valid id, repeated calls
-(the arrival counters reset), an explicit expert map with replicated experts split over ranks,
-and determinism."""
+"""The two-pass decode kernels (AWQ: tp_gate_up_kernel + tp_down_kernel; Q8_0 / Q4_0:
+tp_gate_up_q_kernel + tp_down_q_kernel: one CTA per row tile and piece, weights bulk-copied at
+CTA start, h between the passes in global memory, last-arriver combine per 32-row block) against
+the C oracle, the cluster kernel and the grid-barrier kernel, through the C ABI.  Covers T = 1..8,
+bf16 and fp16 activations, fp32 output, invalid ids, duplicate ids inside a token (more pieces
+than experts), calls with no valid id, repeated calls (the arrival counters reset), an explicit
+expert map with replicated experts split over ranks, and determinism."""
 import numpy as np
 import pytest
 import torch
@@ -17,38 +17,41 @@ pytestmark = pytest.mark.gpu
 if torch.cuda.is_available():
     import moe_ascend_opt_b200  # noqa: F401
     from moe_ascend_opt_b200 import capi
-    from tests.test_gpu_cluster import dev, make_engine, run
+    from tests.test_gpu_cluster import dev, make_engine, oracle, run
 
 AWQ = 2
 SHAPES = [(128, 2048, 768), (32, 1024, 512), (16, 512, 256)]
 
 
+@pytest.mark.parametrize("qt", [AWQ, 1, 0])
 @pytest.mark.parametrize("E,H,I", SHAPES)
 @pytest.mark.parametrize("T", [1, 2, 3, 5, 8])
-def test_two_pass_matches_oracle(E, H, I, T):
-    seed = 2000 + 11 * T + E
-    eng, wts = make_engine(AWQ, E, H, I, seed, two_pass=True)
+def test_two_pass_matches_oracle(qt, E, H, I, T):
+    seed = 2000 + 11 * T + E + qt
+    eng, wts = make_engine(qt, E, H, I, seed, two_pass=True)
     xb, xf, ids, w = tokens(T, H, E, 8, seed)
     y = run(eng, xb, ids, w, H)
-    rel, cos = parity(y, O.moe_forward_awq(xf, ids, w, *wts, group=128))
+    rel, cos = parity(y, oracle(qt, xf, ids, w, wts))
     assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
 
 
+@pytest.mark.parametrize("qt", [AWQ, 1, 0])
 @pytest.mark.parametrize("T", [1, 4])
-def test_two_pass_fp16_activations(T):
+def test_two_pass_fp16_activations(qt, T):
     E, H, I = 32, 1024, 512
-    eng, wts = make_engine(AWQ, E, H, I, 78, two_pass=True)
+    eng, wts = make_engine(qt, E, H, I, 78, two_pass=True)
     xb, xf, ids, w = tokens(T, H, E, 8, 78, bf16=False)
     y = run(eng, xb, ids, w, H, act_bf16=False)
-    rel, cos = parity(y, O.moe_forward_awq(xf, ids, w, *wts, group=128))
+    rel, cos = parity(y, oracle(qt, xf, ids, w, wts))
     assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
 
 
-def test_two_pass_matches_other_kernels():
+@pytest.mark.parametrize("qt", [AWQ, 1])
+def test_two_pass_matches_other_kernels(qt):
     E, H, I = 128, 2048, 768
-    tp, _ = make_engine(AWQ, E, H, I, 5, two_pass=True)
-    cl, _ = make_engine(AWQ, E, H, I, 5)
-    leg, _ = make_engine(AWQ, E, H, I, 5, legacy=True)
+    tp, _ = make_engine(qt, E, H, I, 5, two_pass=True)
+    cl, _ = make_engine(qt, E, H, I, 5)
+    leg, _ = make_engine(qt, E, H, I, 5, legacy=True)
     for T in (1, 4, 8):
         xb, _, ids, w = tokens(T, H, E, 8, 60 + T)
         y = run(tp, xb, ids, w, H)
@@ -57,19 +60,20 @@ def test_two_pass_matches_other_kernels():
             assert rel <= MAX_REL and cos >= MIN_COS, (T, rel, cos)
 
 
-def test_two_pass_odd_routing():
+@pytest.mark.parametrize("qt", [AWQ, 1, 0])
+def test_two_pass_odd_routing(qt):
     """Invalid ids, one expert five times in a token (two pieces at T=3: ncol = 3), a token
     with no valid id, then a call with no valid id at all (zero output), then the first call
     again (counters reset)."""
     E, H, I, T, K = 32, 1024, 512, 3, 8
-    eng, wts = make_engine(AWQ, E, H, I, 9, two_pass=True)
+    eng, wts = make_engine(qt, E, H, I, 9, two_pass=True)
     xb, xf, ids, w = tokens(T, H, E, K, 9)
     ids[0, :5] = 7
     ids[1, 2] = 7
     ids[1, 3] = -1
     ids[2, :] = E + 5
     y = run(eng, xb, ids, w, H)
-    rel, cos = parity(y, O.moe_forward_awq(xf, ids, w, *wts, group=128))
+    rel, cos = parity(y, oracle(qt, xf, ids, w, wts))
     assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
     assert np.all(y[2] == 0.0)
     y0 = run(eng, xb, np.full_like(ids, -3), w, H)
