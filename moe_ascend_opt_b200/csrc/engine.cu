@@ -1651,7 +1651,7 @@ int launch_decode_tp(moe_engine* eng, TpPlan& pl, bool act_bf16, cudaStream_t st
     cfg.dynamicSmemBytes = pl.smem1;
     CUDA_TRY(cudaLaunchKernelEx(&cfg, k1, p));
     cfg.gridDim = dim3(p.H / 32, p.T * p.K);
-    cfg.blockDim = dim3(kTpWarpsB * 32);
+    cfg.blockDim = dim3((qt == MOE_AWQ ? kTpWarpsB : kTpWarpsBQ) * 32);
     cfg.dynamicSmemBytes = pl.smem2;
     CUDA_TRY(cudaLaunchKernelEx(&cfg, k2, p));
     return MOE_OK;

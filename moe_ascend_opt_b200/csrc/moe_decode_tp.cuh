@@ -445,6 +445,7 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_kernel(const TpParams 
 // passes and requantised by every pass-2 CTA for its piece (gemm_kernels.cpp:394-425).
 constexpr int kTpUnitsQ = 16;  // pass 1 (Q8/Q4): gate_up units per CTA, two per warp
 constexpr int kTpCopiesQ = 4;  // its bulk copies
+constexpr int kTpWarpsBQ = 4;  // pass 2 (Q8/Q4) warps per CTA
 
 // The row block's combine by the CTA that completes its arrival count (see the file header).
 MOE_DEV void tp_arrive_combine(const TpParams& p, const TpRoute& rt, int rb, int tid, int nthreads,
@@ -560,20 +561,20 @@ __global__ void __launch_bounds__(kTpWarpsA * 32) tp_gate_up_q_kernel(const TpPa
 // Pass 2 (Q8/Q4): down rows of one 32-row block of one piece (lane = row of the block's
 // row-slice records), weighted into `part`, and the row block's combine.
 template <bool Q4>
-__global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_q_kernel(const TpParams p) {
-    constexpr int kThreads = kTpWarpsB * 32;
+__global__ void __launch_bounds__(kTpWarpsBQ * 32) tp_down_q_kernel(const TpParams p) {
+    constexpr int kThreads = kTpWarpsBQ * 32;
     constexpr int BB = Q4 ? 16 : 32;
     constexpr int SB = 32 * BB + 64;  // row-slice record: 32 rows x one 32-column block, 32 scales
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ TpRoute rt;
-    __shared__ __align__(8) uint64_t bars[kTpWarpsB];
-    __shared__ float red[kTpWarpsB][32][kTpCols];
+    __shared__ __align__(8) uint64_t bars[kTpWarpsBQ];
+    __shared__ float red[kTpWarpsBQ][32][kTpCols];
     __shared__ unsigned int s_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int H = p.H, I = p.I, KB = I >> 5, T = p.T;
     const int rb = blockIdx.x, slot = blockIdx.y;
     TP_STAMP(10);
-    if (tid < kTpWarpsB) mbar_init(&bars[tid], 1);
+    if (tid < kTpWarpsBQ) mbar_init(&bars[tid], 1);
     fence_barrier_init();
     if (warp == 0) tp_route(p, rt, lane);
     __syncthreads();
@@ -597,7 +598,7 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_q_kernel(const TpParam
         return;
     }
     const int e = rt.pe[slot], nc = rt.pn[slot];
-    const int b0 = warp * KB / kTpWarpsB, nbw = (warp + 1) * KB / kTpWarpsB - b0;
+    const int b0 = warp * KB / kTpWarpsBQ, nbw = (warp + 1) * KB / kTpWarpsBQ - b0;
     uint8_t* wd = smem + (size_t)b0 * SB;
     if (lane == 0 && nbw > 0) {
         const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
@@ -638,7 +639,7 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_q_kernel(const TpParam
     float acc[kTpCols];
 #pragma unroll
     for (int m = 0; m < kTpCols; ++m) acc[m] = 0.f;
-    #pragma unroll 1
+    #pragma unroll 2
     for (int r = 0; r < nbw; ++r) {
         const int b = b0 + r;
         const uint8_t* rec = wd + (size_t)r * SB;
@@ -659,11 +660,11 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_q_kernel(const TpParam
     {
         const int r = tid & 31;
 #pragma unroll
-        for (int n = tid >> 5; n < kTpCols; n += kTpWarpsB) {
+        for (int n = tid >> 5; n < kTpCols; n += kTpWarpsBQ) {
             if (n >= nc) continue;
             float v = 0.f;
 #pragma unroll
-            for (int w = 0; w < kTpWarpsB; ++w) v += red[w][r][n];
+            for (int w = 0; w < kTpWarpsBQ; ++w) v += red[w][r][n];
             const int j = rt.pc[slot][n];
             p.part[(size_t)j * H + rb * 32 + r] = __ldg(p.tw + j) * v;
         }
