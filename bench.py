@@ -416,7 +416,11 @@ def run_ours(args):
 
     # N>1, decode sizes: the partials are summed inside the fused kernel over NVLink peer
     # memory (every rank maps every other rank's mailbox); larger T: fp32 partial + NCCL.
-    fused = world > 1 and not args.nccl_combine and handles[0].p2p_covers(T)
+    fused = world > 1 and not args.nccl_combine and not args.dispatch and handles[0].p2p_covers(T)
+    if args.dispatch and world > 1:
+        from moe_ascend_opt_b200.ep import dispatch_forward, expert_owner
+        owner_d = expert_owner(E, world, placement)
+        t_lo, t_hi = rank * T // world, (rank + 1) * T // world  # this rank's own tokens
     if fused:
         for h in handles:
             hnd = h.p2p_mailbox(world, max(T, 8)).to(dev)
@@ -429,6 +433,9 @@ def run_ours(args):
     def step(i):
         h = handles[i % nsets]
         j = i % nin
+        if args.dispatch and world > 1:
+            comp = lambda x, ii, ww: torch.ops.nanovllm.moe_forward_partial(x, ii, ww, h)  # noqa: E731
+            return dispatch_forward(xs[j][t_lo:t_hi], idss[j][t_lo:t_hi], wss[j][t_lo:t_hi], owner_d, world, comp)
         if world == 1 or fused:
             return torch.ops.nanovllm.moe_forward(xs[j], idss[j], wss[j], h)
         part = torch.ops.nanovllm.moe_forward_partial(xs[j], idss[j], wss[j], h)
@@ -536,7 +543,8 @@ def run_ours(args):
                       "parallelism": f"ep{world}" if world > 1 else "single",
                       "placement": args.placement if world > 1 else "n/a",
                       "rank_load_imbalance": imbalance,
-                      "combine": ("in-kernel over NVLink peer memory" if fused else "fp32 partial + NCCL all-reduce")
+                      "combine": ("token all-to-all dispatch + combine (NCCL)" if args.dispatch else
+                                  "in-kernel over NVLink peer memory" if fused else "fp32 partial + NCCL all-reduce")
                       if world > 1 else "in-kernel",
                       "launch": (f"cuda_graph ({ncycle} layer steps per graph replay)" if cycle_graph is not None
                                  else "eager"),
@@ -578,6 +586,11 @@ def run_ours(args):
             j = i % nin
             dbuf.copy_(hbuf[j], non_blocking=True)
             h = handles[i % nsets]
+            if args.dispatch and world > 1:
+                comp = lambda x, ii, ww: torch.ops.nanovllm.moe_forward_partial(x, ii, ww, h)  # noqa: E731
+                y = dispatch_forward(xd[t_lo:t_hi], idd[t_lo:t_hi], wd[t_lo:t_hi], owner_d, world, comp)
+                yh[t_lo:t_hi].copy_(y, non_blocking=True)
+                return
             if world == 1 or fused:
                 y = torch.ops.nanovllm.moe_forward(xd, idd, wd, h)
             else:
@@ -910,6 +923,8 @@ def main():
     ap.add_argument("--sweep-tokens", default="1,4,8,32,128,1024,4096")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1 s clock soak (profiling runs)")
     ap.add_argument("--nccl-combine", action="store_true", help="N>1: fp32 partial + NCCL all-reduce at every T")
+    ap.add_argument("--dispatch", action="store_true",
+                    help="N>1: token-sharded ranks (T/N tokens each), token all-to-all dispatch and combine (NCCL)")
     ap.add_argument("--placement", default="contiguous", choices=["contiguous", "balanced"],
                     help="N>1: experts per rank in contiguous blocks or dealt by routing load")
     ap.add_argument("--cpu-worker", type=float, default=None)

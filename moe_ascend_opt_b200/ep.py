@@ -13,6 +13,13 @@ kernel: each CTA stores its output rows into every rank's mailbox over NVLink an
 (bounded) for the same CTA of the other ranks.
 This replaces the reference's NUMA "TP" split (moe_infer.cpp:143-205,
 q8_gemm.cpp:621-641), whose node-0 reduction becomes the all-reduce.
+
+Token-sharded callers (data-parallel attention: each rank holds its own tokens) use
+`forward_dispatch` instead: every token row is sent once to each rank that owns one of its
+experts (NCCL all-to-all), each rank runs the fused layer on the rows it received (fp32
+partial), and a second all-to-all returns the partials, which the token's rank adds in
+rank order.  The traffic per layer is the routed rows (2 x T x fan-out x H values) instead
+of an all-reduce of the whole [T, H] output.
 """
 from __future__ import annotations
 
@@ -94,6 +101,79 @@ def local_ids(ids: np.ndarray, lo: int, hi: int) -> np.ndarray:
     return np.where((ids >= lo) & (ids < hi), ids - lo, -1).astype(np.int32)
 
 
+def expert_owner(num_experts: int, world: int, placement: Optional[List[List[int]]] = None) -> np.ndarray:
+    """[E] rank holding each global expert: the placement's lists, else contiguous blocks."""
+    own = np.full(num_experts, -1, np.int64)
+    if placement is None:
+        for r, (lo, hi) in enumerate(expert_partition(num_experts, world)):
+            own[lo:hi] = r
+    else:
+        for r, experts in enumerate(placement):
+            for e in experts:
+                if own[e] < 0:  # a replicated expert goes to its first holder
+                    own[e] = r
+    return own
+
+
+def dispatch_plan(topk_ids, owner: np.ndarray, world: int) -> dict:
+    """Rows each rank sends in the token all-to-all: for destination d, the rows (tokens) with
+    at least one expert on d, in token order, and a [rows, K] mask of the pairs d computes
+    (the other ids are sent as -1, which the kernels skip like invalid ids)."""
+    ids = np.asarray(topk_ids.cpu() if hasattr(topk_ids, "cpu") else topk_ids, np.int64)
+    E = owner.shape[0]
+    ok = (ids >= 0) & (ids < E)
+    dest = np.where(ok, owner[np.clip(ids, 0, E - 1)], -1)
+    rows, masks = [], []
+    for d in range(world):
+        m = dest == d
+        r = np.nonzero(m.any(axis=1))[0]
+        rows.append(r)
+        masks.append(m[r])
+    return {"rows": rows, "masks": masks, "dest": dest}
+
+
+def dispatch_forward(hidden, topk_ids, topk_w, owner: np.ndarray, world: int, compute, group=None):
+    """Token all-to-all dispatch and combine over `group` (see ExpertParallelMoE.forward_dispatch):
+    the rows of `dispatch_plan` go out in one all-to-all (hidden, ids with the other ranks' pairs
+    set to -1, weights), `compute(rows, ids, w)` returns the received rows' fp32 partials, a
+    second all-to-all brings them back and they are added per token in rank order."""
+    import torch
+    import torch.distributed as dist
+
+    plan = dispatch_plan(topk_ids, owner, world)
+    dev = hidden.device
+    rows = [torch.as_tensor(r, dtype=torch.long, device=dev) for r in plan["rows"]]
+    ids_t = torch.as_tensor(topk_ids, device=dev)
+    w_t = torch.as_tensor(topk_w, device=dev)
+    send_x = torch.cat([hidden[r] for r in rows])
+    send_i = torch.cat([torch.where(torch.as_tensor(m, device=dev), ids_t[r], torch.full_like(ids_t[r], -1))
+                        for r, m in zip(rows, plan["masks"])])
+    send_w = torch.cat([w_t[r] for r in rows])
+    scount = [len(r) for r in plan["rows"]]
+    sc = torch.tensor(scount, dtype=torch.long, device=dev)
+    rc = torch.empty_like(sc)
+    dist.all_to_all_single(rc, sc, group=group)
+    rcount = [int(v) for v in rc.tolist()]
+    nrecv = sum(rcount)
+    H = hidden.shape[1]
+    recv_x = hidden.new_empty((nrecv, H))
+    recv_i = send_i.new_empty((nrecv, send_i.shape[1]))
+    recv_w = send_w.new_empty((nrecv, send_w.shape[1]))
+    dist.all_to_all_single(recv_x, send_x.contiguous(), rcount, scount, group=group)
+    dist.all_to_all_single(recv_i, send_i.contiguous(), rcount, scount, group=group)
+    dist.all_to_all_single(recv_w, send_w.contiguous(), rcount, scount, group=group)
+    part = compute(recv_x, recv_i, recv_w) if nrecv else torch.zeros((0, H), dtype=torch.float32, device=dev)
+    back = part.new_empty((send_x.shape[0], H))
+    dist.all_to_all_single(back, part.contiguous(), scount, rcount, group=group)
+    y = torch.zeros((hidden.shape[0], H), dtype=torch.float32, device=dev)
+    off = 0
+    for r, n in zip(rows, scount):  # rank order: deterministic sums
+        if n:
+            y[r] += back[off:off + n]
+        off += n
+    return y.to(hidden.dtype)
+
+
 class ExpertParallelMoE:
     """Fused MoE layer with experts sharded over a process group.
 
@@ -110,6 +190,9 @@ class ExpertParallelMoE:
         import moe_ascend_opt_b200  # noqa: F401  (registers torch.classes.nanovllm)
 
         self.group = group
+        self.num_experts = num_experts
+        self.placement = placement
+        self.replicas = list(replicas or [])
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.lo, self.hi = expert_partition(num_experts, self.world)[self.rank]
@@ -152,6 +235,23 @@ class ExpertParallelMoE:
         self.peers = True
 
     peers = False
+
+    def expert_owner(self) -> np.ndarray:
+        """[E] rank holding each global expert (from the placement, else the contiguous blocks)."""
+        return expert_owner(self.num_experts, self.world, self.placement)
+
+    def forward_dispatch(self, hidden, topk_ids, topk_w, compute=None):
+        """Token all-to-all dispatch and combine: `hidden` [T_r, H], `topk_ids` / `topk_w`
+        [T_r, K] are this rank's own tokens (global expert ids); returns this rank's [T_r, H]
+        output.  `compute(rows, ids, w) -> fp32 [N, H]` runs the layer over this rank's experts
+        (default: moe_forward_partial on this rank's engine)."""
+        import torch
+
+        if self.replicas:
+            raise ValueError("forward_dispatch sends each pair to one rank; build the layer without replicas")
+        if compute is None:
+            compute = lambda x, i, w: torch.ops.nanovllm.moe_forward_partial(x, i, w, self.handle)  # noqa: E731
+        return dispatch_forward(hidden, topk_ids, topk_w, self.expert_owner(), self.world, compute, self.group)
 
     def forward(self, hidden, topk_ids, topk_w, out: Optional[object] = None):
         import torch

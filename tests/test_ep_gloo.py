@@ -166,3 +166,57 @@ def test_replicated_partials_sum_to_full_forward(qt):
                                 dd[ex]) for r, ex in enumerate(pl))
     full = O.moe_forward_q(qt, False, xf, ids, w, gq, gd, dq, dd)
     assert float(np.abs(total - full).max() / np.abs(full).max()) < 1e-5
+
+
+def _dispatch_worker(rank, world, port, placed, result_q):
+    from oracle import oracle as O
+    from tests.helpers import q_weights, tokens
+    from moe_ascend_opt_b200.ep import balanced_placement, dispatch_forward, expert_owner, local_ids_map
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    E, H, I, K = 16, 256, 128, 8
+    counts = [5, 3, 0, 2][:world]  # token-sharded: each rank its own tokens (one rank none at 4)
+    T = counts[rank]
+    gq, gd, dq, dd = q_weights(1, E, H, I, 41)
+    _, xf_all, ids_all, w_all = tokens(sum(counts), H, E, K, 41)
+    off = sum(counts[:rank])
+    xf, ids, w = xf_all[off:off + T].copy(), ids_all[off:off + T].copy(), w_all[off:off + T].copy()
+    if rank == 0 and T:
+        ids[0, :3] = 9      # an expert three times in a token
+        ids[1, 2] = -1      # invalid ids travel as -1
+    placement = balanced_placement(np.bincount(ids_all.ravel(), minlength=E), world) if placed else None
+    owner = expert_owner(E, world, placement)
+    mine = placement[rank] if placed else list(range(rank * E // world, (rank + 1) * E // world))
+    sel = np.asarray(mine)
+
+    def compute(x, i, wt):  # this rank's experts over the received rows (the engine's role)
+        li = local_ids_map(i.numpy(), mine)
+        return torch.from_numpy(O.moe_forward_q(1, False, x.numpy(), li, wt.numpy(),
+                                                gq[sel], gd[sel], dq[sel], dd[sel]))
+
+    y = dispatch_forward(torch.from_numpy(xf), torch.from_numpy(ids), torch.from_numpy(w), owner, world, compute)
+    full = O.moe_forward_q(1, False, xf, ids, w, gq, gd, dq, dd) if T else np.zeros((0, H), np.float32)
+    err = float(np.abs(y.numpy() - full).max() / max(np.abs(full).max(), 1e-30)) if T else 0.0
+    result_q.put((rank, err, tuple(y.shape)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,placed", [(2, False), (2, True), (4, True)])
+def test_token_all_to_all_dispatch(world, placed):
+    """Token-sharded ranks (5, 3 and 0 tokens): every routed row goes to the ranks owning its
+    experts, the partials come back and each rank's output equals the single-rank forward of
+    its own tokens (contiguous blocks, load-balanced placement, a rank with no tokens)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dispatch_worker, args=(r, world, port, placed, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    assert all(p.exitcode == 0 for p in procs)
+    res = sorted(q.get(timeout=5) for _ in range(world))
+    for rank, err, shape in res:
+        assert err <= 1e-5, (rank, err)

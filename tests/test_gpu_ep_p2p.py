@@ -78,3 +78,48 @@ def test_two_rank_peer_combine_matches_oracle(qt, sk_min):
                 assert np.array_equal(a, y0[0])  # both ranks, every repeat: the same bits
             rel, cos = parity(y0[0], y_ref)
             assert rel <= MAX_REL and cos >= MIN_COS, (T, rel, cos)
+
+
+def _dispatch_worker(rank, world, port, outdir, E, H, I, K, T):
+    import torch.distributed as dist
+
+    from tests.helpers import awq_weights
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    import moe_ascend_opt_b200  # noqa: F401
+    from moe_ascend_opt_b200.ep import ExpertParallelMoE
+
+    wts = awq_weights(E, H, I, 128, 7)
+    moe = ExpertParallelMoE(E, H, I, 2)
+    moe.load_awq(*[torch.from_numpy(a) for a in wts])
+    xb, _, ids, w = tokens(T, H, E, K, 7)
+    lo, hi = rank * T // world, (rank + 1) * T // world  # this rank's own tokens
+    x = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)[lo:hi]
+    y = moe.forward_dispatch(x, torch.from_numpy(ids[lo:hi]).cuda(), torch.from_numpy(w[lo:hi]).cuda())
+    torch.cuda.synchronize()
+    assert moe.handle.device_error() == 0
+    np.save(os.path.join(outdir, f"d_{rank}.npy"), y.float().cpu().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("T", [2, 37])
+def test_two_rank_token_dispatch_awq_matches_oracle(T):
+    """Token-sharded ranks, token all-to-all dispatch and combine over NCCL (AWQ, the MiniMax
+    format): each rank's rows equal the oracle's rows for its own tokens."""
+    import torch.multiprocessing as mp
+
+    from oracle import oracle as O
+    from tests.helpers import awq_weights
+
+    E, H, I, K = 32, 1024, 512, 8
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_dispatch_worker, args=(2, _free_port(), d, E, H, I, K, T), nprocs=2, join=True)
+        _, xf, ids, w = tokens(T, H, E, K, 7)
+        y_ref = O.moe_forward_awq(xf, ids, w, *awq_weights(E, H, I, 128, 7), group=128)
+        y = np.concatenate([np.load(os.path.join(d, f"d_{r}.npy")) for r in range(2)])
+        rel, cos = parity(y, y_ref)
+        assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
