@@ -93,7 +93,9 @@ def _dispatch_worker(rank, world, port, outdir, E, H, I, K, T):
 
     wts = awq_weights(E, H, I, 128, 7)
     moe = ExpertParallelMoE(E, H, I, 2)
-    moe.load_awq(*[torch.from_numpy(a) for a in wts])
+    t = [torch.from_numpy(np.ascontiguousarray(a)) for a in wts]
+    t[1], t[4] = t[1].view(torch.int16).view(torch.bfloat16), t[4].view(torch.int16).view(torch.bfloat16)
+    moe.load_awq(*t)  # the torch class takes the scales as bfloat16 tensors
     xb, _, ids, w = tokens(T, H, E, K, 7)
     lo, hi = rank * T // world, (rank + 1) * T // world  # this rank's own tokens
     x = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)[lo:hi]
