@@ -188,6 +188,8 @@ __global__ void __launch_bounds__(kTpWarpsA * 32) tp_gate_up_kernel(const TpPara
     const int H = p.H, I = p.I, NK1 = H / kAwqK;
     const int tile = blockIdx.x, slot = blockIdx.y;
     TP_STAMP(0);
+    // L2 policy of the weight copies, made before the dependency wait (off the critical path)
+    const uint64_t pol = (lane == 0 && (p.flags & kFlagEvictFirst)) ? l2_evict_first_policy() : 0ull;
     if (tid < 2 * kTpWarpsA) mbar_init(&bars[tid], 1);
     fence_barrier_init();
     tp_dep_wait(warp);
@@ -231,7 +233,6 @@ __global__ void __launch_bounds__(kTpWarpsA * 32) tp_gate_up_kernel(const TpPara
     if (lane == 0 && warp < 2 * kTpCopiesA) {
         const int half = warp / kTpCopiesA, i = warp % kTpCopiesA;
         const int r0 = i * NK1 / kTpCopiesA, n = (i + 1) * NK1 / kTpCopiesA - r0;
-        const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
         const size_t rec0 = (((size_t)e * (I / 16) + tile) * 2 + half) * NK1 + r0;
         if (n > 0)
             issue_copy((half ? wu : wg) + (size_t)r0 * kAwqGuRec, p.gu + rec0 * kAwqGuRec, (uint32_t)n * kAwqGuRec,
@@ -306,6 +307,7 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_kernel(const TpParams 
     const int H = p.H, I = p.I, NKD = I / kAwqK, T = p.T, K = p.K;
     const int rb = blockIdx.x, slot = blockIdx.y;
     TP_STAMP(10);
+    const uint64_t pol = (lane == 0 && (p.flags & kFlagEvictFirst)) ? l2_evict_first_policy() : 0ull;
     if (tid < kTpWarpsB) mbar_init(&bars[tid], 1);
     fence_barrier_init();
     if (warp == 0) tp_route(p, rt, lane);
@@ -336,7 +338,6 @@ __global__ void __launch_bounds__(kTpWarpsB * 32) tp_down_kernel(const TpParams 
     const int k0 = warp * NKD / kTpWarpsB, nk = (warp + 1) * NKD / kTpWarpsB - k0;
     uint8_t* wd = smem + (size_t)k0 * kAwqDnRec;
     if (lane == 0 && nk > 0) {
-        const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
         const size_t rec0 = ((size_t)e * (H / 32) + rb) * NKD + k0;
         issue_copy(wd, p.dn + rec0 * kAwqDnRec, (uint32_t)nk * kAwqDnRec, &bars[warp], pol);
     }
@@ -495,6 +496,8 @@ __global__ void __launch_bounds__(kTpWarpsA * 32) tp_gate_up_q_kernel(const TpPa
     const int ub = 2 * (p.rs1 + p.ss1);
     const int tile = blockIdx.x, slot = blockIdx.y;
     TP_STAMP(0);
+    // L2 policy of the weight copies, made before the dependency wait (off the critical path)
+    const uint64_t pol = (lane == 0 && (p.flags & kFlagEvictFirst)) ? l2_evict_first_policy() : 0ull;
     if (tid < kTpCopiesQ) mbar_init(&bars[tid], 1);
     fence_barrier_init();
     tp_dep_wait(warp);
@@ -513,7 +516,6 @@ __global__ void __launch_bounds__(kTpWarpsA * 32) tp_gate_up_q_kernel(const TpPa
     const int u0 = tile * kTpUnitsQ, nu = min(kTpUnitsQ, I - u0);
     if (lane == 0 && warp < kTpCopiesQ) {
         const int a = warp * nu / kTpCopiesQ, n = (warp + 1) * nu / kTpCopiesQ - a;
-        const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
         if (n > 0)
             issue_copy(smem + (size_t)a * ub, p.gu + ((size_t)e * I + u0 + a) * ub, (uint32_t)n * ub, &bars[warp], pol);
         else
@@ -574,6 +576,7 @@ __global__ void __launch_bounds__(kTpWarpsBQ * 32) tp_down_q_kernel(const TpPara
     const int H = p.H, I = p.I, KB = I >> 5, T = p.T;
     const int rb = blockIdx.x, slot = blockIdx.y;
     TP_STAMP(10);
+    const uint64_t pol = (lane == 0 && (p.flags & kFlagEvictFirst)) ? l2_evict_first_policy() : 0ull;
     if (tid < kTpWarpsBQ) mbar_init(&bars[tid], 1);
     fence_barrier_init();
     if (warp == 0) tp_route(p, rt, lane);
@@ -601,7 +604,6 @@ __global__ void __launch_bounds__(kTpWarpsBQ * 32) tp_down_q_kernel(const TpPara
     const int b0 = warp * KB / kTpWarpsBQ, nbw = (warp + 1) * KB / kTpWarpsBQ - b0;
     uint8_t* wd = smem + (size_t)b0 * SB;
     if (lane == 0 && nbw > 0) {
-        const uint64_t pol = (p.flags & kFlagEvictFirst) ? l2_evict_first_policy() : 0ull;
         issue_copy(wd, p.dn + (((size_t)e * (H / 32) + rb) * KB + b0) * SB, (uint32_t)nbw * SB, &bars[warp], pol);
     }
     TP_STAMP(12);
