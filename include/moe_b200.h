@@ -152,13 +152,18 @@ int moe_quantize_rows_q8_0(const void* x, int32_t dtype, int64_t rows, int64_t c
                            float* d, void* stream);
 
 /* Diagnostics (no counterpart in the reference): enable != 0 makes every later decode
- * launch record 20 stamps per CTA (globaltimer ns unless noted; phase boundaries of the
- * fused kernel: start, routing, activation quantisation, first/last gate_up data, gate_up
- * done, grid barrier entered/passed, h requantised, first down data, down done, combine
- * done, SM clock at start/end, first down issue (split-K kernel: its chunk count and h
- * slots), barrier arrival fenced/observed, warp 0 down loop done / first down wait);
+ * launch record 20 stamps per CTA (globaltimer ns unless noted).  Persistent decode kernels
+ * (one row per SM): phase boundaries of the fused kernel: start, routing, activation
+ * quantisation, first/last gate_up data, gate_up done, grid barrier entered/passed, h
+ * requantised, first down data, down done, combine done, SM clock at start/end, first down
+ * issue (split-K kernel: its chunk count and h slots), barrier arrival fenced/observed, warp 0
+ * down loop done / first down wait.  Two-pass kernels (one row per CTA of the grid, row =
+ * slot x tiles + tile; pass 1 in entries 0-9: start, dependency wait passed, routed and
+ * tokens staged, weight copies issued, [AWQ: weight data], end; pass 2 in entries 10-19: start,
+ * routed, copies issued, dependency wait passed, h staged, weight data, dots done, arrival,
+ * combine done).  Rows beyond the buffer's (at least 1024) are not recorded.
  * enable == 0 turns it off.  When `out` is non-null, copies up to max_entries stamps of
- * the last launch (waits for the device).  *n_entries = CTAs x 20 while enabled. */
+ * the last launch (waits for the device).  *n_entries = rows x 20 while enabled. */
 int moe_engine_debug_timeline(moe_engine* eng, int32_t enable, uint64_t* out, int32_t max_entries,
                               int32_t* n_entries);
 
