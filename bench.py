@@ -52,17 +52,15 @@ def tflops_peaks():
 
 def path_kernels(quant, T, K, E, peer_combine=False):
     """(kernel(s) of the layer's path, launches per layer step) under the engine's default
-    dispatch: AWQ up to 8 tokens the two-pass kernels, up to 24 the grid-barrier decode kernel,
-    beyond that the tcgen05 grouped GEMMs; Q8_0 / Q4_0 up to 4 tokens the two-pass kernels, up to
+    dispatch: AWQ up to 32 tokens the two-pass kernels (in slices of 8 tokens), beyond that the
+    tcgen05 grouped GEMMs; Q8_0 / Q4_0 up to 4 tokens the two-pass kernels, up to
     8 the split-K decode kernel, beyond that the grouped GEMMs (route, quantise, two GEMMs,
     combine)."""
     if peer_combine:
         return "moe_decode_kernel (peer combine)", 1
     if quant == "awq":
-        if T <= 8:
-            return "tp_gate_up_kernel + tp_down_kernel", 2
-        if T <= 24:
-            return "moe_decode_kernel", 1
+        if T <= 32:  # slices of 8 tokens
+            return "tp_gate_up_kernel + tp_down_kernel", 2 * ((T + 7) // 8)
         return "grouped_gemm_tc_kernel", 7
     if T <= 4:
         return "tp_gate_up_q_kernel + tp_down_q_kernel", 2

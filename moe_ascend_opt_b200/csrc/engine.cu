@@ -63,6 +63,7 @@ struct moe_engine {
     uint8_t* agu = nullptr;
     uint8_t* adn = nullptr;
     int tp_max_tokens = -1;  // two-pass decode kernels (tp_gate_up / tp_down) up to this many tokens (-1: by format)
+    int tp_slice_max = -1;   // and in slices of tp_max_tokens up to this many (-1: by format)
     int cl_max_tokens = -1;  // cluster decode kernel (moe_decode_cl_kernel) up to this many tokens (-1: by format)
     int cl_size = 4;         // its CTAs per cluster
     bool pdl = true;         // launch it with programmatic stream serialization
@@ -1400,6 +1401,8 @@ extern "C" int moe_engine_create(const moe_config* cfg, moe_engine** out) {
     if (eng->cl_max_tokens < 0) eng->cl_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 1;  // where it is faster
     if (const char* v = std::getenv("MOE_TP_MAX_TOKENS")) eng->tp_max_tokens = std::atoi(v);
     if (eng->tp_max_tokens < 0) eng->tp_max_tokens = cfg->quant_type == MOE_AWQ ? 8 : 4;  // where it is faster
+    if (const char* v = std::getenv("MOE_TP_SLICE_MAX")) eng->tp_slice_max = std::atoi(v);
+    if (eng->tp_slice_max < 0) eng->tp_slice_max = cfg->quant_type == MOE_AWQ ? 32 : 0;  // measured crossover
     int rc = MOE_OK;
     rc = alloc_q_layout(eng);
     if (rc == MOE_OK) rc = ensure_workspace(eng, 64);
@@ -1711,6 +1714,45 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
     const size_t xe = 2, ye = out_dtype == MOE_F32 ? 4 : 2;
     if (eng->p2p_active && !moe_engine_p2p_covers(eng, T))
         return fail(MOE_ERR_STATE, "peer combine covers decode-size calls only; use the fp32 partial and an all-reduce");
+    // decode sizes: the two-pass kernels, in token slices of at most tp_max_tokens up to
+    // tp_slice_max tokens (each slice's pass 1 waits for the previous slice's pass 2)
+    if (!eng->p2p_active && (T <= eng->tp_max_tokens || T <= eng->tp_slice_max) && eng->tp_max_tokens > 0) {
+        const int64_t S = std::min<int64_t>(T, eng->tp_max_tokens);
+        TpPlan tp;
+        if (plan_decode_tp(eng, (int)S, (int)K, tp)) {
+            if (int rc = ensure_clpart(eng, S * K)) return rc;   // part [S K][H]
+            if (int rc = ensure_workspace(eng, S * K)) return rc;  // h, counters, error word
+            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+            CUDA_TRY(cudaStreamIsCapturing(st, &cap));
+            const bool timed = cap == cudaStreamCaptureStatusNone;
+            if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
+            const size_t ye = out_dtype == MOE_F32 ? 4 : 2;
+            for (int64_t t0 = 0; t0 < T; t0 += S) {
+                const int64_t n = std::min(S, T - t0);
+                if (n != S && !plan_decode_tp(eng, (int)n, (int)K, tp)) return fail(MOE_ERR_INVALID, "plan failed");
+                TpParams& p = tp.p;
+                p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
+                p.act_bf16 = act_dtype == MOE_BF16;
+                p.x = static_cast<const uint8_t*>(x) + (size_t)t0 * H * 2;
+                p.y = static_cast<uint8_t*>(y) + (size_t)t0 * H * ye;
+                p.ids = topk_ids + t0 * K;
+                p.tw = topk_w + t0 * K;
+                p.gu = eng->cfg.quant_type == MOE_AWQ ? eng->agu : eng->gu;
+                p.dn = eng->adn;
+                p.h = eng->h_ws;
+                p.part = eng->clpart;
+                p.cnt = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(eng->bar) + 256);
+                p.err = eng->err;
+                p.dbg = eng->timeline_ctas >= (int)(std::max<int64_t>(H / 32, p.I / 16) * n * K) ? eng->timeline : nullptr;
+                if (int rc = launch_decode_tp(eng, tp, act_dtype == MOE_BF16, st)) return rc;
+            }
+            if (timed) {
+                CUDA_TRY(cudaEventRecord(eng->ev1, st));
+                eng->timed = true;
+            }
+            return MOE_OK;
+        }
+    }
     if (T > eng->awq_gemm_min_tokens && awq_gemm_ok(eng)) {  // AWQ: the tcgen05 GEMMs on the 16-bit rows
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
         CUDA_TRY(cudaStreamIsCapturing(st, &cap));
@@ -1740,36 +1782,7 @@ extern "C" int moe_engine_forward(moe_engine* eng, const void* x, void* y, const
         }
         return MOE_OK;
     }
-    // decode sizes: the two-pass kernels, else the cluster kernel, when they apply
-    if (!eng->p2p_active && T <= eng->tp_max_tokens) {
-        TpPlan tp;
-        if (plan_decode_tp(eng, (int)T, (int)K, tp)) {
-            if (int rc = ensure_clpart(eng, T * K)) return rc;   // part [T K][H]
-            if (int rc = ensure_workspace(eng, T * K)) return rc;  // h, counters, error word
-            cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-            CUDA_TRY(cudaStreamIsCapturing(st, &cap));
-            const bool timed = cap == cudaStreamCaptureStatusNone;
-            if (timed) CUDA_TRY(cudaEventRecord(eng->ev0, st));
-            TpParams& p = tp.p;
-            p.out_kind = out_dtype == MOE_F32 ? 2 : (out_dtype == MOE_BF16 ? 1 : 0);
-            p.act_bf16 = act_dtype == MOE_BF16;
-            p.x = x; p.y = y; p.ids = topk_ids; p.tw = topk_w;
-            p.gu = eng->cfg.quant_type == MOE_AWQ ? eng->agu : eng->gu;
-            p.dn = eng->adn;
-            p.h = eng->h_ws;
-            p.part = eng->clpart;
-            p.cnt = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(eng->bar) + 256);
-            p.err = eng->err;
-            p.dbg = eng->timeline_ctas >= (int)(std::max<int64_t>(H / 32, p.I / 16) * T * K) ? eng->timeline : nullptr;
-            const int rc = launch_decode_tp(eng, tp, act_dtype == MOE_BF16, st);
-            if (rc) return rc;
-            if (timed) {
-                CUDA_TRY(cudaEventRecord(eng->ev1, st));
-                eng->timed = true;
-            }
-            return MOE_OK;
-        }
-    }
+    // decode sizes: the cluster kernel when it applies
     if (!eng->p2p_active && T <= eng->cl_max_tokens) {
         ClPlan cp;
         const int qt = eng->cfg.quant_type;

@@ -134,3 +134,15 @@ def test_two_pass_deterministic_and_graph():
     torch.cuda.synchronize()
     assert eng.device_error() == 0
     assert np.array_equal(y.float().cpu().numpy(), outs[0])
+
+
+@pytest.mark.parametrize("T", [12, 20, 32])
+def test_two_pass_token_slices_awq(T):
+    """AWQ calls of 9-32 tokens run the two-pass kernels in slices of 8 tokens (each slice's
+    pass 1 waits for the previous slice's pass 2 through the stream)."""
+    E, H, I = 32, 1024, 512
+    eng, wts = make_engine(AWQ, E, H, I, 300 + T, two_pass=True)
+    xb, xf, ids, w = tokens(T, H, E, 8, 300 + T)
+    y = run(eng, xb, ids, w, H)
+    rel, cos = parity(y, oracle(AWQ, xf, ids, w, wts))
+    assert rel <= MAX_REL and cos >= MIN_COS, (rel, cos)
