@@ -50,6 +50,12 @@ def tflops_peaks():
         return 1400.0
 
 
+# DRAM bytes per layer step measured by ncu for the workloads that were captured (mean over 10
+# launches each): (format, shape, tokens) -> tp_gate_up + tp_down read + write bytes (Q4_0
+# 14,203,443 + 7,154,739; AWQ 13,817,651 + 6,936,243); algorithmic 21,233,664 and 19,611,648.
+NCU_TRAFFIC = {("q4", "qwen", 1): 21358182, ("awq", "qwen", 1): 20753894}
+
+
 def path_kernels(quant, T, K, E, peer_combine=False):
     """(kernel(s) of the layer's path, launches per layer step) under the engine's default
     dispatch: AWQ up to 32 tokens the two-pass kernels (in slices of 8 tokens), beyond that the
@@ -554,7 +560,10 @@ def run_ours(args):
     if True:
         out["roofline"] = {"bound": "hbm", "achieved": round(value, 2), "peak": peak, "unit": "GB/s",
                            "frac": round(value / peak, 4), "peak_source": peak_kind,
-                           "traffic": None,
+                           "traffic": NCU_TRAFFIC.get((args.quant, args.shape, T)) if world == 1 else None,
+                           "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of both kernels, one "
+                                              "capture of this workload (same command, --steps 50)")
+                           if world == 1 and (args.quant, args.shape, T) in NCU_TRAFFIC else None,
                            "algorithmic_bytes_per_launch": round(avg_bytes),
                            "kernel": path_kernels(args.quant, T, K, E, world > 1 and fused)[0]}
     # end-to-end through the public op with host buffers and copies in the timed region
@@ -790,6 +799,7 @@ def extra_block(quant, shape, routing, T, steps, dev, peak, nsets=16):
            "avg_active_experts": round(avg_b / bpe, 2),
            "roofline": {"bound": "hbm", "achieved": round(val, 2), "peak": peak, "unit": "GB/s",
                         "frac": round(val / peak, 4), "algorithmic_bytes_per_launch": round(avg_b),
+                        "traffic": NCU_TRAFFIC.get((quant, shape, T)),
                         "kernel": path_kernels(quant, T, K, E_)[0]},
            "launch": f"cuda_graph ({ncyc} layer steps per replay, {nsets} weight sets)"}
     if errs:
